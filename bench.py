@@ -1,0 +1,377 @@
+"""Decode-attention benchmark: KV-read TB/s and us per decode step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload config2]
+
+One step = one decode call over one batch: every sequence's K/V is read once.
+N=1 workload: config 2 (fp16 varlen + sinks, B=32, QH=32, KVH=8, D=128, lens
+U[8192,16384] seed 0; 1.545 GB of KV, larger than L2, so no flush is needed).
+N>1 (torchrun, one process per GPU, NCCL): weak scaling -- rank r decodes its
+own config-2 batch drawn with seed r; no collective on the data path, the
+step time is the max over ranks.  ``--workload config5`` instead shards the
+config-5 batch (B=128 e4m3 paged) across ranks by greedy LPT (strong scaling).
+
+``value`` is whole-job KV bytes / device time (TB/s), timed with CUDA events
+around K back-to-back steps, bracketed by barriers and synchronisation.
+``e2e`` is the same metric through the public API with the per-step inputs
+(q and the sequence lengths) copied from pinned host memory and the output
+copied back inside the timed region; the KV cache is resident on the GPU, as
+in a serving engine.  ``--impl reference`` times the CPU restatement of the
+reference's torch attention (the only CPU implementation of this path) on
+the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from fasterkernels_b200 import workloads as W  # noqa: E402
+
+METRIC = "decode-attn KV-read TB/s"
+UNIT = "TB/s"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            if len(r) >= 9:
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- workloads
+def setup_workload(name, rank, world, device):
+    """Build this rank's share of the workload on `device`.  Returns a dict
+    with a zero-arg `run()` (one decode step through the public API), the
+    per-step inputs for the e2e leg, algorithmic KV bytes and a config dict."""
+    import fasterkernels_b200 as fk
+    if name == "config2":
+        spec = W.CONFIGS[2]
+        lens = W.config_lengths(2, seed=rank)
+        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
+        q, k, v, cu, s = d["q"], d["k"], d["v"], d["cu_seqlens"], d["s_aux"]
+        out = torch.empty_like(q)
+
+        def run(qq=q, cc=cu, oo=out):
+            return fk.flash_decode_gqa_varlen(qq, k, v, cc, s, out=oo)
+        kvb = W.kv_bytes(lens, spec.kv_heads, 2)
+        cfg = {"workload": spec.name, "batch_per_gpu": spec.batch, "global_batch": spec.batch * world,
+               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
+               "seq_lens": "U[8192,16384], seed = rank", "tokens_this_rank": int(sum(lens)),
+               "kv_layout": "contiguous varlen [T, KV_H, D] fp16", "sinks": True,
+               "l2": "inputs larger than L2 (>=1.5 GB KV per GPU, no flush)",
+               "parallelism": f"dp{world} (each rank its own batch, no collective)"}
+        return dict(run=run, q=q, lens_dev=cu, out=out, kv_bytes=kvb, cfg=cfg, scaling="weak",
+                    sample=(q, k, v, cu, s, lens), dtype="fp16 in / fp32 accumulate")
+    if name == "config5":
+        spec = W.CONFIGS[5]
+        all_lens = W.config_lengths(5, seed=0)
+        mine = W.lpt_partition(all_lens, world)[rank]
+        lens = [all_lens[i] for i in mine]
+        # KV drawn in fp16 on the device, then quantised per tensor to e4m3
+        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
+        k8, sk = W.quantize_e4m3(d["k"])
+        del d["k"]
+        v8, sv = W.quantize_e4m3(d["v"])
+        del d["v"]
+        kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=rank)
+        del k8, v8
+        kp, vp = kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn)
+        q, s = d["q"], d["s_aux"]
+        sl = torch.tensor(lens, dtype=torch.int32, device=device)
+        out = torch.empty_like(q)
+
+        def run(qq=q, ll=sl, oo=out):
+            return fk.paged_flash_decode(qq, kp, vp, bt, ll, 16, s_aux=s, scale_k=sk, scale_v=sv, out=oo)
+        kvb = W.kv_bytes(lens, spec.kv_heads, 1)
+        cfg = {"workload": spec.name, "global_batch": spec.batch, "batch_this_rank": len(lens),
+               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
+               "seq_lens": "logU[4096,131072] seed 0, LPT-sharded by KV bytes",
+               "kv_layout": "paged 16-token pages, e4m3 KV, fp16 Q", "sinks": True,
+               "l2": "inputs larger than L2", "parallelism": f"sequence-sharded x{world}, no collective"}
+        return dict(run=run, q=q, lens_dev=sl, out=out, kv_bytes=kvb, cfg=cfg, scaling="strong",
+                    sample=None, dtype="e4m3 KV / fp16 Q / fp32 accumulate")
+    raise SystemExit(f"unknown workload {name}")
+
+
+def cpu_sample_rate(sample, min_seconds=8.0, max_seqs=2):
+    """Time the CPU oracle (numpy fp32, all BLAS threads) on the first
+    `max_seqs` sequences of the batch; returns (TB/s of fp16 KV bytes, desc)."""
+    from oracle import gqa_decode_oracle as O
+    q, k, v, cu, s, lens = sample
+    n = min(max_seqs, len(lens))
+    hi = int(cu[n])
+    qn = q[:n].float().cpu().numpy()
+    kn = k[:hi].cpu().numpy()
+    vn = v[:hi].cpu().numpy()
+    cun = cu[: n + 1].cpu().numpy()
+    sn = None if s is None else s.cpu().numpy()
+    byt = W.kv_bytes(lens[:n], k.shape[1], 2)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.decode_varlen(qn, kn, vn, cun, sn, dtype=np.float32)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return byt * reps / el / 1e12, f"{n} sequences ({hi} tokens) x {reps} reps, numpy fp32"
+
+
+# ---------------------------------------------------------------- our arm
+def time_steps(fn, steps, stream):
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        fn()
+    ev1.record(stream)
+    ev1.synchronize()
+    return ev0.elapsed_time(ev1)
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_ours(args, rank, world, local_rank):
+    from fasterkernels_b200 import _native as N
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    wl = setup_workload(args.workload, rank, world, device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(args.warmup, 3)):
+        wl["run"]()
+    torch.cuda.synchronize()
+    if N.read_status(device) != 0:
+        raise SystemExit("device status word set during warm-up")
+
+    # ---- headline: K back-to-back steps, inputs resident in HBM
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = time_steps(wl["run"], args.steps, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms_step = max_over_ranks(ms / args.steps, world, device)
+    tot_bytes = sum_over_ranks(float(wl["kv_bytes"]), world, device)
+    value = tot_bytes / (ms_step * 1e-3) / 1e12
+
+    # ---- split-kernel duration (library events on the launching stream)
+    N.profile_begin(args.steps)
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        wl["run"]()
+    split_ms, comb_ms, n = N.profile_end()
+    split_avg = split_ms / max(n, 1)
+    comb_avg = comb_ms / max(n, 1)
+
+    # ---- e2e: pinned host q + lengths in, output back, every step
+    q_h = wl["q"].cpu().pin_memory()
+    l_h = wl["lens_dev"].cpu().pin_memory()
+    o_h = torch.empty(wl["out"].shape, dtype=wl["out"].dtype).pin_memory()
+
+    def e2e_step():
+        wl["q"].copy_(q_h, non_blocking=True)
+        wl["lens_dev"].copy_(l_h, non_blocking=True)
+        wl["run"]()
+        o_h.copy_(wl["out"], non_blocking=True)
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e_ms = time_steps(e2e_step, args.steps, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_step = max_over_ranks(e_ms / args.steps, world, device)
+    h2d = q_h.numel() * q_h.element_size() + l_h.numel() * l_h.element_size()
+    d2h = o_h.numel() * o_h.element_size()
+    if N.read_status(device) != 0:
+        raise SystemExit("device status word set during the timed region")
+
+    if rank != 0:
+        return None
+    peak, peak_kind = load_peaks()
+    achieved = wl["kv_bytes"] / (split_avg * 1e-3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            tr = json.load(f).get(args.workload)
+            if tr:
+                traffic = tr["bytes_per_launch"]
+    except Exception:
+        pass
+    rec = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_step": round(ms_step * 1e3, 2),
+        "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": wl["dtype"],
+        "data": "synthetic (seeded N(0,1) q/k/v/s_aux; no dataset)", "config": wl["cfg"],
+        "roofline": {"bound": "hbm", "kernel": "decode_split_kernel", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s", "traffic": traffic,
+                     "split_us": round(split_avg * 1e3, 2), "combine_us": round(comb_avg * 1e3, 2),
+                     "hbm_frac_whole_step": round(wl["kv_bytes"] / (ms / args.steps * 1e-3) / 1e9 / peak, 4)},
+        "e2e": {"value": round(tot_bytes / (e_step * 1e-3) / 1e12, 4), "unit": UNIT,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e_step, 5),
+                "note": "public API; q and lengths H2D from pinned memory and output D2H each step; KV resident"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+    if world == 1 and wl["sample"] is not None and not args.no_cpu_baseline:
+        cpu_val, desc = cpu_sample_rate(wl["sample"])
+        rec["cpu_baseline"] = {"value": round(cpu_val, 6), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                               "sample": desc + " (CPU restatement of the reference's torch ref_attention)"}
+    return rec
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    """The reference's CPU implementation of the path: its torch attention
+    formula, restated in numpy (oracle/gqa_decode_oracle.py), on all host
+    threads.  Rank 0 only; each step is a bounded sample of the workload."""
+    if rank != 0:
+        return None
+    from oracle import gqa_decode_oracle as O
+    if args.workload != "config2":
+        spec = W.CONFIGS[5]
+        lens = W.config_lengths(5, seed=0)
+        kvh, qh, es = spec.kv_heads, spec.q_heads, 1
+    else:
+        spec = W.CONFIGS[2]
+        lens = W.config_lengths(2, seed=0)
+        kvh, qh, es = spec.kv_heads, spec.q_heads, 2
+    L = lens[0]
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, qh, 128, generator=g).numpy()
+    k = torch.randn(L, kvh, 128, generator=g).half().numpy()
+    v = torch.randn(L, kvh, 128, generator=g).half().numpy()
+    s = torch.randn(qh, generator=g).numpy()
+    cu = np.array([0, L])
+    byt = W.kv_bytes([L], kvh, es)
+    for _ in range(args.warmup):
+        O.decode_varlen(q, k, v, cu, s, dtype=np.float32)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.decode_varlen(q, k, v, cu, s, dtype=np.float32)
+    el = time.perf_counter() - t0
+    val = byt * args.steps / el / 1e12
+    cores = os.cpu_count()
+    desc = f"sequence 0 of the workload ({L} tokens, KV_H={kvh}) per step, numpy fp32 BLAS"
+    return {"impl": "reference", "metric": METRIC, "value": round(val, 6), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak" if args.workload == "config2" else "strong",
+            "vs_baseline": None, "dtype": "fp32 (CPU)", "data": "synthetic",
+            "config": {"workload": spec.name, "sample": desc},
+            "cpu_baseline": {"value": round(val, 6), "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+            "e2e": {"value": round(val, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["config2", "config5"], default="config2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        rec = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        rec = run_ours(args, rank, world, local_rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if rec is not None:
+        print(json.dumps(rec), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,171 @@
+"""ctypes binding of the C-ABI in include/fk_decode.h, plus the per-device
+workspace and the torch-tensor -> C-argument plumbing shared by the entry
+points.  torch supplies device memory and the current stream only; every
+decode runs in the sm_100a kernels of ``_lib/libfk_decode.so``.  There is no
+fallback: if the library is missing or fails, the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from .build import LIB_PATH
+
+FK_DTYPE_F16 = 0
+FK_DTYPE_BF16 = 1
+FK_DTYPE_E4M3 = 2
+
+FK_STATUS_BAD_PAGE = 1
+FK_STATUS_TIMEOUT = 2
+
+_DTYPE_CODES = {
+    torch.float16: FK_DTYPE_F16,
+    torch.bfloat16: FK_DTYPE_BF16,
+    torch.float8_e4m3fn: FK_DTYPE_E4M3,
+}
+
+_lib = None
+_lib_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_int64
+_Z = ctypes.c_size_t
+
+
+def lib() -> ctypes.CDLL:
+    """Load the native library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"fasterkernels_b200 native library not found at {LIB_PATH}; build it with "
+                "`python -m fasterkernels_b200.build` (needs nvcc with sm_100a support)")
+        L = ctypes.CDLL(LIB_PATH)
+        L.fk_version.restype = _I
+        L.fk_version.argtypes = []
+        L.fk_last_error.restype = ctypes.c_char_p
+        L.fk_last_error.argtypes = []
+        L.fk_decode_workspace_bytes.restype = _Z
+        L.fk_decode_workspace_bytes.argtypes = [_I, _I, _I, _I]
+        L.fk_flash_decode_gqa_varlen.restype = _I
+        L.fk_flash_decode_gqa_varlen.argtypes = [
+            _P, _P, _P, _P, _P, _P,          # q k v cu s_aux out
+            _I, _I, _I, _I, _L, _I,          # batch q_heads kv_heads head_dim total_tokens dtype
+            _L, _L, _L, _L, _L, _L, _L, _L,  # strides
+            _P, _Z, _P]
+        L.fk_flash_decode_gqa_hf_dense.restype = _I
+        L.fk_flash_decode_gqa_hf_dense.argtypes = [
+            _P, _P, _P, _P, _P, _P, _P,      # q k v cache_lens starts s_aux out
+            _I, _I, _I, _I, _L,              # batch q_heads kv_heads head_dim max_seqlen
+            _I, _I, _I,                      # q_dtype kv_dtype out_dtype
+            _P, _P, _P,                      # scales
+            _L, _L, _L, _L, _L, _L, _L, _L, _L, _L,
+            _P, _Z, _P]
+        L.fk_paged_flash_decode.restype = _I
+        L.fk_paged_flash_decode.argtypes = [
+            _P, _P, _P, _P, _P, _P, _P,      # q k v bt seq_lens s_aux out
+            _I, _I, _I, _I, _L, _I, _I,      # batch q_heads kv_heads head_dim num_pages page_size max_blocks
+            _I, _I, _I,                      # dtypes
+            _P, _P, _P,                      # scales
+            _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L,
+            _P, _Z, _P]
+        L.fk_profile_begin.restype = _I
+        L.fk_profile_begin.argtypes = [_I]
+        L.fk_profile_end.restype = _I
+        L.fk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
+                                     ctypes.POINTER(_I)]
+        L.fk_decode_num_ctas.restype = _I
+        L.fk_decode_num_ctas.argtypes = [_I, _I]
+        _lib = L
+        return L
+
+
+def last_error() -> str:
+    msg = lib().fk_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed (code {rc}): {last_error()}")
+
+
+def dtype_code(t: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[t]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t}; expected float16, bfloat16 or float8_e4m3fn") from None
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+# ---------------------------------------------------------------- workspace
+_ws = {}
+_ws_retired = []
+_ws_lock = threading.Lock()
+
+
+def workspace(device: torch.device, batch: int, kv_heads: int, kv_dtype_code: int) -> torch.Tensor:
+    """The cached per-device workspace, grown to fit (batch, kv_heads).
+
+    Grown only outside CUDA-graph capture: a graph replays the pointer it
+    captured, so run one eager call with the largest batch before capturing.
+    Calls on one device share it, so they must be stream-ordered.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    need = int(lib().fk_decode_workspace_bytes(idx, batch, kv_heads, kv_dtype_code))
+    if need == 0:
+        raise RuntimeError(f"fk_decode_workspace_bytes failed: {last_error()}")
+    with _ws_lock:
+        ws = _ws.get(idx)
+        if ws is None or ws.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(
+                    "decode workspace must be allocated before CUDA graph capture: run one eager "
+                    "decode call with the captured batch size first")
+            if ws is not None:
+                _ws_retired.append(ws)  # a captured graph may still point at it
+            size = max(need, 0 if ws is None else ws.numel() * 2)
+            ws = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+            _ws[idx] = ws
+        return ws
+
+
+def read_status(device=None, clear: bool = True) -> int:
+    """Read (and by default clear) the sticky FK_STATUS_* word of a device's
+    workspace.  Synchronises with the device; keep it off the hot path."""
+    idx = torch.cuda.current_device() if device is None else torch.device(device).index
+    ws = _ws.get(idx)
+    if ws is None:
+        return 0
+    st = int(ws[:4].view(torch.int32).item())
+    if clear:
+        ws[:4].zero_()
+    return st
+
+
+def profile_begin(max_launches: int) -> None:
+    """Record CUDA events around the split and combine passes of the next
+    ``max_launches`` decode calls (on their launching streams)."""
+    check(lib().fk_profile_begin(int(max_launches)), "fk_profile_begin")
+
+
+def profile_end():
+    """Stop recording; returns (split_ms_total, combine_ms_total, calls)."""
+    a, b, n = ctypes.c_float(), ctypes.c_float(), ctypes.c_int()
+    check(lib().fk_profile_end(ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)), "fk_profile_end")
+    return a.value, b.value, n.value

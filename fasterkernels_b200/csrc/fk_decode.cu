@@ -1,0 +1,1088 @@
+// fk_decode.cu -- B200 (sm_100a) GQA decode attention: split pass + combine
+// pass, behind the C-ABI declared in include/fk_decode.h.
+//
+// Work decomposition ("stream-K" over KV granules).  Every (sequence b,
+// KV head h) pair is an item owning ceil(len_b / 16) granules of 16 tokens;
+// items are laid end to end (b-major, h minor) into one stream of
+// U = kv_heads * sum_b ceil(len_b/16) granules, and CTA c of the persistent
+// grid (S CTAs, S = resident CTAs on the device) takes granules
+// [c*per, (c+1)*per) with per = max(ceil(U/S), 4).  Every CTA therefore
+// streams the same number of KV bytes whatever the length distribution, and
+// the plan is derived on the device from the lengths alone (no host sync,
+// CUDA-graph safe).  The piece of item i inside CTA c is a segment with id
+// c + i (unique, < S + items).  A CTA that holds a whole item normalises and
+// writes the output itself; otherwise it stores the segment's (max, sum,
+// acc) partial and the combine kernel merges the partials of that item with
+// the sink term.
+//
+// Split pass, per CTA: one producer warp walks the plan and issues TMA tile
+// loads (64 tokens x 128 dims of K and of V per stage, 128-byte swizzled)
+// into an mbarrier ring; four consumer warps each take 16 tokens of every
+// tile and run QK^T and PV on the tensor cores with mma.sync m16n8k16,
+// tokens as the M dimension and the G <= 8 query heads of the KV group as N,
+// keeping a private online-softmax state that is merged across the warps at
+// the end of each segment.  FP8 e4m3 K/V are widened to f16 in registers;
+// scale_k folds into the logit scale and scale_v into the final output.
+//
+// Layouts (address policies of the producer):
+//   VARLEN  k[T, KVH, 128]          3-D tensor map, coords (d, h, t)
+//   DENSE   k[B, KVH, S, 128]       4-D tensor map, coords (d, s, h, b)
+//   PAGED   pool[P, KVH, 16, 128]   4-D tensor map, coords (d, 0, h, page)
+// The plan, the tile sequence and the arithmetic do not depend on the
+// layout, so paged and contiguous results are bit-identical.
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/fk_decode.h"
+#include "fk_ptx.cuh"
+
+namespace fk {
+
+constexpr int HEAD_DIM = 128;
+constexpr int GPAD = 8;        // MMA N: query heads of one KV group, padded
+constexpr int TILE = 64;       // tokens per pipeline stage
+constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
+constexpr int THREADS = (CWARPS + 1) * 32;
+constexpr int PAGE = 16;       // tokens per granule (= page size)
+constexpr int MIN_PER = 4;     // minimum granules per CTA (one tile)
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float NEG_INF = -__builtin_huge_valf();
+
+enum Layout { VARLEN = 0, DENSE = 1, PAGED = 2 };
+enum Flags { F_FIRST = 1, F_LAST = 2, F_WHOLE = 4, F_END = 8 };
+
+template <int KV>
+struct KvCfg {
+  static constexpr bool FP8 = (KV == FK_DTYPE_E4M3);
+  static constexpr bool BF16 = (KV == FK_DTYPE_BF16);
+  static constexpr int ES = FP8 ? 1 : 2;                     // bytes per element
+  static constexpr int TILE_BYTES = TILE * HEAD_DIM * ES;    // K (or V) bytes per stage
+  static constexpr int PAGE_BYTES = PAGE * HEAD_DIM * ES;    // one page of K (or V)
+  static constexpr int STAGES = FP8 ? 4 : 5;
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  static constexpr int BOX_D = FP8 ? 128 : 64;               // dims per TMA box (128 bytes)
+  static constexpr int NHALF = HEAD_DIM / BOX_D;             // boxes per 128-dim row
+  static constexpr int HALF_BYTES = TILE * 128;              // one [64 rows][128 B] box region
+};
+
+struct Meta {
+  int b, h, tok, valid, flags, seg, bad, pad;
+};
+
+// Workspace layout (bytes): [0, 256) header, then pre[B+1] (int32 exclusive
+// prefix of granules per sequence), then ml[(S+I)*8] float2, then
+// acc[(S+I)*8*128] float.
+struct WsHeader {
+  int status;
+  int pad0;
+  long long per;
+};
+
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  size_t pre, ml, acc, total;
+  __host__ __device__ WsLayout(int B, int kvh, int S) {
+    size_t segs = static_cast<size_t>(S) + static_cast<size_t>(B) * kvh;
+    pre = 256;
+    ml = align_up(pre + 4 * (static_cast<size_t>(B) + 1), 256);
+    acc = align_up(ml + segs * GPAD * sizeof(float2), 256);
+    total = align_up(acc + segs * GPAD * HEAD_DIM * sizeof(float), 256);
+  }
+};
+
+struct Params {
+  CUtensorMap tk;  // K tensor map (64-byte aligned, first member)
+  CUtensorMap tv;  // V tensor map
+  const void* q;
+  long long q_sb, q_sh;
+  void* out;
+  long long o_sb, o_sh;
+  const int* lens;    // VARLEN: cu_seqlens[B+1]; DENSE: cache_lens[B]; PAGED: seq_lens[B]
+  const int* starts;  // DENSE: start_k_offsets[B] or null
+  const int* bt;      // PAGED: block table
+  long long bt_sb;
+  long long max_tokens;  // DENSE: cache rows per sequence
+  int max_blocks, num_pages;
+  const float* s_aux;
+  const float* scale_q;
+  const float* scale_k;
+  const float* scale_v;
+  unsigned char* ws;
+  int B, q_heads, kv_heads, G;
+  int q_dtype, out_dtype;
+  int num_ctas;
+};
+
+// Effective length of sequence b and the coordinate of its first token.
+template <int LAYOUT>
+__device__ __forceinline__ int seq_len(const Params& p, int b, long long* tok0) {
+  if constexpr (LAYOUT == VARLEN) {
+    const int s = __ldg(p.lens + b), e = __ldg(p.lens + b + 1);
+    *tok0 = s;
+    return max(e - s, 0);
+  } else if constexpr (LAYOUT == DENSE) {
+    const int s = p.starts ? max(__ldg(p.starts + b), 0) : 0;
+    const long long e = min(static_cast<long long>(__ldg(p.lens + b)), p.max_tokens);
+    *tok0 = s;
+    return static_cast<int>(max(e - s, 0ll));
+  } else {
+    *tok0 = 0;
+    return max(__ldg(p.lens + b), 0);
+  }
+}
+
+__device__ __forceinline__ long long warp_incl_scan(long long v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+__device__ __forceinline__ float load_q_elem(const Params& p, long long idx, float sq) {
+  if (p.q_dtype == FK_DTYPE_F16) return __half2float(static_cast<const __half*>(p.q)[idx]);
+  if (p.q_dtype == FK_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p.q)[idx]);
+  const __nv_fp8_storage_t v = static_cast<const __nv_fp8_storage_t*>(p.q)[idx];
+  const __half_raw hr = __nv_cvt_fp8_to_halfraw(v, __NV_E4M3);
+  return __half2float(__half(hr)) * sq;
+}
+
+__device__ __forceinline__ void store_out(const Params& p, long long idx, float v) {
+  if (p.out_dtype == FK_DTYPE_BF16)
+    static_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half*>(p.out)[idx] = __float2half_rn(v);
+}
+
+// Normalisation of one (query head, dim) output with the oracle's sink
+// formula.  A, L are relative to the running max M (log2 domain).
+__device__ __forceinline__ float finalize(float A, float L, float M, const float* s_aux, int qh, float sv) {
+  if (s_aux != nullptr) {
+    const float s2 = __ldg(s_aux + qh) * LOG2E;
+    const float Ms = fmaxf(M, s2);
+    const float e = exp2f(M - Ms);
+    A *= e;
+    L = L * e + exp2f(s2 - Ms);
+  }
+  return L > 0.f ? (A / L) * sv : 0.f;
+}
+
+// ------------------------------------------------------------------------
+// Split pass.
+// ------------------------------------------------------------------------
+template <int KV, int LAYOUT>
+__global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_constant__ Params p) {
+  using C = KvCfg<KV>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* stages = smem;
+  float* cacc = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);        // [CWARPS][GPAD][128]
+  float* cm = cacc + CWARPS * GPAD * HEAD_DIM;                                      // [CWARPS][GPAD]
+  float* cl = cm + CWARPS * GPAD;                                                   // [CWARPS][GPAD]
+  Meta* meta = reinterpret_cast<Meta*>(cl + CWARPS * GPAD);                          // [STAGES]
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + C::STAGES);                   // [STAGES]
+  uint64_t* empty = full + C::STAGES;                                               // [STAGES]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  WsHeader* hdr = reinterpret_cast<WsHeader*>(p.ws);
+  const WsLayout wl(p.B, p.kv_heads, p.num_ctas);
+  int* pre = reinterpret_cast<int*>(p.ws + wl.pre);
+  float2* ws_ml = reinterpret_cast<float2*>(p.ws + wl.ml);
+  float* ws_acc = reinterpret_cast<float*>(p.ws + wl.acc);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), CWARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == CWARPS) {
+    // ================================================================ producer
+    if (lane == 0) {
+      prefetch_tmap(&p.tk);
+      prefetch_tmap(&p.tv);
+    }
+    const long long KVH = p.kv_heads;
+    // Plan: total granules and (CTA 0 only) the per-sequence prefix.
+    long long tot = 0;
+    for (int base = 0; base < p.B; base += 32) {
+      const int b = base + lane;
+      long long t0;
+      const long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
+      const long long inc = warp_incl_scan(n, lane);
+      if (blockIdx.x == 0 && b < p.B) pre[b] = static_cast<int>(tot + inc - n);
+      tot += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    const long long U = tot * KVH;
+    const long long S = p.num_ctas;
+    const long long per = max((U + S - 1) / S, static_cast<long long>(MIN_PER));
+    if (blockIdx.x == 0 && lane == 0) {
+      pre[p.B] = static_cast<int>(tot);
+      hdr->per = per;
+    }
+    const long long start = static_cast<long long>(blockIdx.x) * per;
+    const long long end = min(start + per, U);
+
+    int stage = 0;
+    uint32_t phase = 0;
+    bool alive = true;
+    // Claim the next ring slot (waits for the consumers to release it).
+    auto acquire = [&]() -> bool {
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(smem_u32(&empty[stage]), phase ^ 1u) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok && lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
+      return ok != 0;
+    };
+    auto advance = [&]() {
+      if (++stage == C::STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    };
+
+    if (start < end) {
+      // Locate the first item of this CTA's granule range.
+      int bs = -1;
+      long long preb = 0, run = 0;
+      for (int base = 0; base < p.B && bs < 0; base += 32) {
+        const int b = base + lane;
+        long long t0;
+        const long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
+        const long long inc = warp_incl_scan(n, lane);
+        const bool hit = (b < p.B) && (KVH * (run + inc) > start);
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        if (m) {
+          const int L = __ffs(m) - 1;
+          bs = base + L;
+          preb = run + __shfl_sync(0xffffffffu, inc - n, L);
+        }
+        run += __shfl_sync(0xffffffffu, inc, 31);
+      }
+      int b = bs;
+      long long tok0;
+      int len = seq_len<LAYOUT>(p, b, &tok0);
+      long long nb = (len + PAGE - 1) / PAGE;
+      int h = static_cast<int>((start - KVH * preb) / nb);
+      long long item_base = KVH * preb + static_cast<long long>(h) * nb;
+      long long pos = start;
+
+      // PAGED: window of 32 block-table entries (one per lane) + the next one.
+      int win_b = -1;
+      int win_p0 = 0;
+      int bt_cur = -1, bt_nxt = -1;
+      auto ld_bt = [&](int bb, int pg) -> int {
+        return (pg < p.max_blocks) ? __ldg(p.bt + static_cast<long long>(bb) * p.bt_sb + pg) : -1;
+      };
+
+      while (alive && pos < end) {
+        const long long seg_hi = min(end, item_base + nb);
+        const int g0 = static_cast<int>(pos - item_base);
+        const int g1 = static_cast<int>(seg_hi - item_base);
+        const bool whole = (item_base >= start) && (item_base + nb <= end);
+        const int seg = blockIdx.x + b * p.kv_heads + h;
+        const int tbeg = g0 * PAGE;
+        const int tend = min(g1 * PAGE, len);
+        for (int tt = tbeg; tt < tend; tt += TILE) {
+          const int valid = min(TILE, tend - tt);
+          if (!acquire()) {
+            alive = false;
+            break;
+          }
+          const uint32_t sK = smem_u32(stages + stage * C::STAGE_BYTES);
+          const uint32_t sV = sK + C::TILE_BYTES;
+          const uint32_t fb = smem_u32(&full[stage]);
+          int bad = 0;
+          uint32_t bytes = 2u * C::TILE_BYTES;
+          int phys = -1;
+          int np = 0;
+          if constexpr (LAYOUT == PAGED) {
+            const int p0 = tt / PAGE;
+            np = (valid + PAGE - 1) / PAGE;
+            if (b != win_b || p0 < win_p0 || p0 + 4 > win_p0 + 32) {
+              if (b == win_b && p0 == win_p0 + 32) {
+                bt_cur = bt_nxt;
+                win_p0 += 32;
+              } else {
+                win_b = b;
+                win_p0 = p0;
+                bt_cur = ld_bt(b, p0 + lane);
+              }
+              bt_nxt = ld_bt(b, win_p0 + 32 + lane);
+            }
+            phys = __shfl_sync(0xffffffffu, bt_cur, (p0 - win_p0) + (lane & 3));
+            const bool okp = (lane < np) && phys >= 0 && phys < p.num_pages;
+            const unsigned okm = __ballot_sync(0xffffffffu, okp) & 0xfu;
+            bad = static_cast<int>(~okm & ((1u << np) - 1u));
+            bytes = static_cast<uint32_t>(__popc(okm)) * 2u * C::PAGE_BYTES;
+            if (lane == 0 && bad) atomicOr(&hdr->status, FK_STATUS_BAD_PAGE);
+            if (!okp) phys = -1;
+          }
+          if (lane == 0) {
+            Meta& mt = meta[stage];
+            mt.b = b;
+            mt.h = h;
+            mt.tok = tt;
+            mt.valid = valid;
+            mt.flags = (tt == tbeg ? F_FIRST : 0) | (tt + TILE >= tend ? F_LAST : 0) | (whole ? F_WHOLE : 0);
+            mt.seg = seg;
+            mt.bad = bad;
+            mbar_arrive_expect_tx(fb, bytes);
+          }
+          __syncwarp();
+          if constexpr (LAYOUT == PAGED) {
+            if (phys >= 0) {
+#pragma unroll
+              for (int hf = 0; hf < C::NHALF; ++hf) {
+                const uint32_t off = hf * C::HALF_BYTES + lane * (PAGE * 128);
+                tma_load_4d(sK + off, &p.tk, fb, hf * C::BOX_D, 0, h, phys);
+                tma_load_4d(sV + off, &p.tv, fb, hf * C::BOX_D, 0, h, phys);
+              }
+            }
+          } else if (lane == 0) {
+#pragma unroll
+            for (int hf = 0; hf < C::NHALF; ++hf) {
+              const uint32_t off = hf * C::HALF_BYTES;
+              if constexpr (LAYOUT == VARLEN) {
+                const int row = static_cast<int>(tok0 + tt);
+                tma_load_3d(sK + off, &p.tk, fb, hf * C::BOX_D, h, row);
+                tma_load_3d(sV + off, &p.tv, fb, hf * C::BOX_D, h, row);
+              } else {
+                const int row = static_cast<int>(tok0 + tt);
+                tma_load_4d(sK + off, &p.tk, fb, hf * C::BOX_D, row, h, b);
+                tma_load_4d(sV + off, &p.tv, fb, hf * C::BOX_D, row, h, b);
+              }
+            }
+          }
+          advance();
+        }
+        pos = seg_hi;
+        if (pos >= end) break;
+        if (++h == p.kv_heads) {
+          h = 0;
+          do {
+            preb += nb;
+            ++b;
+            len = seq_len<LAYOUT>(p, b, &tok0);
+            nb = (len + PAGE - 1) / PAGE;
+          } while (nb == 0 && b + 1 < p.B);
+        }
+        item_base = KVH * preb + static_cast<long long>(h) * nb;
+      }
+    }
+    // End-of-work marker.
+    if (alive && acquire()) {
+      if (lane == 0) {
+        meta[stage].flags = F_END;
+        mbar_arrive(smem_u32(&full[stage]));
+      }
+    }
+    return;
+  }
+
+  // ================================================================ consumers
+  constexpr bool FP8 = C::FP8;
+  constexpr bool MBF16 = C::BF16;  // MMA element type (FP8 KV computes in f16)
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int r0 = warp * 16;
+  const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
+  const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
+  const float sq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
+  const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
+
+  float m[2], l[2], acc[8][4];
+  uint32_t qb[8][2];
+  int stage = 0;
+  uint32_t phase = 0;
+
+  // Thread-constant shared-memory offsets.
+  const int lr = lane & 7, lq = lane >> 3;
+  // 16-bit path: ldmatrix row addresses.
+  const int krow = r0 + lr + ((lq & 1) << 3);
+  const int vrow = r0 + lr + ((lq >> 1) << 3);
+  // FP8 path: logical token g <-> tile row prow (and prow + 8); V rows
+  // r0 + t + 4(r&1) + 8(r>>1); V dim chunk cg.
+  const int prow = r0 + (g >> 1) + ((g & 1) << 2);
+  const int cg = (g >> 1) | ((g & 1) << 2);
+
+  while (true) {
+    if (!mbar_wait(smem_u32(&full[stage]), phase)) {
+      if (lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
+      break;
+    }
+    const Meta mt = meta[stage];
+    if (mt.flags & F_END) break;
+
+    if (mt.flags & F_FIRST) {
+      m[0] = m[1] = NEG_INF;
+      l[0] = l[1] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      const bool hv = g < p.G;
+      const long long qbase = static_cast<long long>(mt.b) * p.q_sb + static_cast<long long>(mt.h * p.G + g) * p.q_sh;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        int d0, d1;
+        if constexpr (FP8) {
+          d0 = (j < 4) ? (16 * t + 4 * j) : (64 + 16 * t + 4 * (j - 4));
+          d1 = d0 + 2;
+        } else {
+          d0 = 16 * j + 2 * t;
+          d1 = d0 + 8;
+        }
+        float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+        if (hv) {
+          x0 = load_q_elem(p, qbase + d0, sq);
+          x1 = load_q_elem(p, qbase + d0 + 1, sq);
+          x2 = load_q_elem(p, qbase + d1, sq);
+          x3 = load_q_elem(p, qbase + d1 + 1, sq);
+        }
+        qb[j][0] = pack2<MBF16>(x0, x1);
+        qb[j][1] = pack2<MBF16>(x2, x3);
+      }
+    }
+
+    if (r0 < mt.valid) {
+      const uint32_t sK = smem_u32(stages + stage * C::STAGE_BYTES);
+      const uint32_t sV = sK + C::TILE_BYTES;
+      const bool partial = (r0 + 16 > mt.valid) || (mt.bad != 0);
+      auto tok_ok = [&](int row) -> bool { return row < mt.valid && !((mt.bad >> (row >> 4)) & 1); };
+
+      // ---- S^T = K Q^T : 16 tokens x 8 heads
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      int rowA, rowB;
+      if constexpr (FP8) {
+        rowA = prow;
+        rowB = prow + 8;
+        const int sw = prow & 7;
+        const uint32_t ra = sK + prow * 128, rb = ra + 8 * 128;
+        const uint4 alo = lds128(ra + ((t ^ sw) << 4));
+        const uint4 ahi = lds128(ra + (((t + 4) ^ sw) << 4));
+        const uint4 blo = lds128(rb + ((t ^ sw) << 4));
+        const uint4 bhi = lds128(rb + (((t + 4) ^ sw) << 4));
+        const uint32_t wa[8] = {alo.x, alo.y, alo.z, alo.w, ahi.x, ahi.y, ahi.z, ahi.w};
+        const uint32_t wb[8] = {blo.x, blo.y, blo.z, blo.w, bhi.x, bhi.y, bhi.z, bhi.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t a0 = e4m3x2_to_f16x2(wa[j]);
+          const uint32_t a2 = e4m3x2_to_f16x2(wa[j] >> 16);
+          const uint32_t a1 = e4m3x2_to_f16x2(wb[j]);
+          const uint32_t a3 = e4m3x2_to_f16x2(wb[j] >> 16);
+          mma16816<false>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
+        }
+      } else {
+        rowA = r0 + g;
+        rowB = r0 + g + 8;
+        const uint32_t kb = sK + krow * 128;
+        const int ksw = krow & 7;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = ((j & 3) << 1) + (lq >> 1);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(kb + (j >> 2) * C::HALF_BYTES + ((c ^ ksw) << 4), a0, a1, a2, a3);
+          mma16816<MBF16>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
+        }
+      }
+
+      // ---- online softmax (log2 domain), heads 2t and 2t+1
+      const bool okA = tok_ok(rowA), okB = tok_ok(rowB);
+      const float x0 = okA ? s[0] * qk_scale : NEG_INF;
+      const float x1 = okA ? s[1] * qk_scale : NEG_INF;
+      const float x2 = okB ? s[2] * qk_scale : NEG_INF;
+      const float x3 = okB ? s[3] * qk_scale : NEG_INF;
+      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+      const float b0s = (mn0 == NEG_INF) ? 0.f : mn0;
+      const float b1s = (mn1 == NEG_INF) ? 0.f : mn1;
+      const float al0 = exp2f(m[0] - b0s), al1 = exp2f(m[1] - b1s);
+      const float p0 = exp2f(x0 - b0s), p1 = exp2f(x1 - b1s);
+      const float p2 = exp2f(x2 - b0s), p3 = exp2f(x3 - b1s);
+      l[0] = l[0] * al0 + (p0 + p2);
+      l[1] = l[1] * al1 + (p1 + p3);
+      m[0] = mn0;
+      m[1] = mn1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[i][0] *= al0;
+        acc[i][1] *= al1;
+        acc[i][2] *= al0;
+        acc[i][3] *= al1;
+      }
+      // P^T as the B operand: transpose the 8x8 (token x head) blocks.
+      const uint32_t pb0 = movmatrix_t(pack2<MBF16>(p0, p1));
+      const uint32_t pb1 = movmatrix_t(pack2<MBF16>(p2, p3));
+
+      // ---- O^T += V^T P^T : 128 dims x 8 heads
+      if constexpr (FP8) {
+        uint4 x[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int row = r0 + t + 4 * (r & 1) + 8 * (r >> 1);
+          x[r] = lds128(sV + row * 128 + ((cg ^ (row & 7)) << 4));
+          if (partial && !tok_ok(row)) x[r] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        const uint32_t w0[4] = {x[0].x, x[0].y, x[0].z, x[0].w};
+        const uint32_t w1[4] = {x[1].x, x[1].y, x[1].z, x[1].w};
+        const uint32_t w2[4] = {x[2].x, x[2].y, x[2].z, x[2].w};
+        const uint32_t w3[4] = {x[3].x, x[3].y, x[3].z, x[3].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t sel = (i & 1) ? 0x7362u : 0x5140u;
+          const uint32_t u01 = __byte_perm(w0[i >> 1], w1[i >> 1], sel);
+          const uint32_t u89 = __byte_perm(w2[i >> 1], w3[i >> 1], sel);
+          mma16816<false>(acc[i], e4m3x2_to_f16x2(u01), e4m3x2_to_f16x2(u01 >> 16), e4m3x2_to_f16x2(u89),
+                          e4m3x2_to_f16x2(u89 >> 16), pb0, pb1);
+        }
+      } else {
+        uint32_t mk01 = 0xffffffffu, mk89 = 0xffffffffu;
+        if (partial) {
+          const int tk = r0 + 2 * t;
+          mk01 = (tok_ok(tk) ? 0x0000ffffu : 0u) | (tok_ok(tk + 1) ? 0xffff0000u : 0u);
+          mk89 = (tok_ok(tk + 8) ? 0x0000ffffu : 0u) | (tok_ok(tk + 9) ? 0xffff0000u : 0u);
+        }
+        const uint32_t vb = sV + vrow * 128;
+        const int vsw = vrow & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = ((2 * i) & 7) + (lq & 1);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(vb + (i >> 2) * C::HALF_BYTES + ((c ^ vsw) << 4), a0, a1, a2, a3);
+          mma16816<MBF16>(acc[i], a0 & mk01, a1 & mk01, a2 & mk89, a3 & mk89, pb0, pb1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
+
+    if (mt.flags & F_LAST) {
+      // ---- merge the four warps' states for this segment
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        l[0] += __shfl_xor_sync(0xffffffffu, l[0], o);
+        l[1] += __shfl_xor_sync(0xffffffffu, l[1], o);
+      }
+      if (g == 0) {
+        cm[warp * GPAD + 2 * t] = m[0];
+        cm[warp * GPAD + 2 * t + 1] = m[1];
+        cl[warp * GPAD + 2 * t] = l[0];
+        cl[warp * GPAD + 2 * t + 1] = l[1];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int d = FP8 ? (16 * cg + 2 * i + r) : (16 * i + g + 8 * r);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int hd = 2 * t + j;
+            if (hd < p.G) cacc[(warp * GPAD + hd) * HEAD_DIM + d] = acc[i][2 * r + j];
+          }
+        }
+      }
+      named_bar_sync(1, CWARPS * 32);
+      const int d = threadIdx.x;  // 0..127
+      for (int hd = 0; hd < p.G; ++hd) {
+        float M = NEG_INF;
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, cm[w * GPAD + hd]);
+        float A = 0.f, L = 0.f;
+        if (M != NEG_INF) {
+#pragma unroll
+          for (int w = 0; w < CWARPS; ++w) {
+            const float mw = cm[w * GPAD + hd];
+            const float e = exp2f(mw - M);
+            A += e * cacc[(w * GPAD + hd) * HEAD_DIM + d];
+            L += e * cl[w * GPAD + hd];
+          }
+        }
+        const int qh = mt.h * p.G + hd;
+        if (mt.flags & F_WHOLE) {
+          const float o = finalize(A, L, M, p.s_aux, qh, sv);
+          store_out(p, static_cast<long long>(mt.b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d, o);
+        } else {
+          ws_acc[(static_cast<long long>(mt.seg) * GPAD + hd) * HEAD_DIM + d] = A;
+          if (d == 0) ws_ml[static_cast<long long>(mt.seg) * GPAD + hd] = make_float2(M, L);
+        }
+      }
+      named_bar_sync(1, CWARPS * 32);
+    }
+    if (++stage == C::STAGES) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
+// Combine pass: one CTA (128 threads = head dims) per (sequence, KV head).
+// Merges the segment partials of items that span several CTAs and writes
+// the all-zero rows of empty sequences.
+// ------------------------------------------------------------------------
+template <int LAYOUT>
+__global__ void __launch_bounds__(128) decode_combine_kernel(const __grid_constant__ Params p) {
+  const int item = blockIdx.x;
+  const int b = item / p.kv_heads;
+  const int h = item % p.kv_heads;
+  const int d = threadIdx.x;
+  const WsHeader* hdr = reinterpret_cast<const WsHeader*>(p.ws);
+  const WsLayout wl(p.B, p.kv_heads, p.num_ctas);
+  const int* pre = reinterpret_cast<const int*>(p.ws + wl.pre);
+  const float2* ws_ml = reinterpret_cast<const float2*>(p.ws + wl.ml);
+  const float* ws_acc = reinterpret_cast<const float*>(p.ws + wl.acc);
+  long long tok0;
+  const int len = seq_len<LAYOUT>(p, b, &tok0);
+  const long long nb = (len + PAGE - 1) / PAGE;
+  if (nb == 0) {
+    for (int hd = 0; hd < p.G; ++hd) {
+      const int qh = h * p.G + hd;
+      store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d, 0.f);
+    }
+    return;
+  }
+  const long long per = hdr->per;
+  const long long P = static_cast<long long>(p.kv_heads) * pre[b] + static_cast<long long>(h) * nb;
+  const long long c0 = P / per, c1 = (P + nb - 1) / per;
+  if (c0 == c1) return;  // written by the split pass
+  const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
+  for (int hd = 0; hd < p.G; ++hd) {
+    float M = NEG_INF;
+    for (long long c = c0; c <= c1; ++c) M = fmaxf(M, ws_ml[(c + item) * GPAD + hd].x);
+    float A = 0.f, L = 0.f;
+    if (M != NEG_INF) {
+      for (long long c = c0; c <= c1; ++c) {
+        const float2 ml = ws_ml[(c + item) * GPAD + hd];
+        const float e = exp2f(ml.x - M);
+        A += e * ws_acc[((c + item) * GPAD + hd) * HEAD_DIM + d];
+        L += e * ml.y;
+      }
+    }
+    const int qh = h * p.G + hd;
+    store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d,
+              finalize(A, L, M, p.s_aux, qh, sv));
+  }
+}
+
+// ------------------------------------------------------------------------
+// Host side.
+// ------------------------------------------------------------------------
+thread_local std::string g_err;
+
+// Optional per-launch timing: when enabled, three events are recorded on the
+// launching stream around each split pass and combine pass.
+struct Profiler {
+  std::mutex mu;
+  bool on = false;
+  int cap = 0, n = 0;
+  cudaEvent_t* ev = nullptr;  // 3 per launch
+};
+Profiler g_prof;
+
+void prof_mark(int which, cudaStream_t stream) {
+  if (!g_prof.on) return;
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (!g_prof.on || g_prof.n >= g_prof.cap) return;
+  cudaEventRecord(g_prof.ev[3 * g_prof.n + which], stream);
+  if (which == 2) ++g_prof.n;
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+template <int KV>
+constexpr size_t smem_bytes() {
+  using C = KvCfg<KV>;
+  return 1024 + C::STAGES * C::STAGE_BYTES + sizeof(float) * (CWARPS * GPAD * HEAD_DIM + 2 * CWARPS * GPAD) +
+         sizeof(Meta) * C::STAGES + 2 * sizeof(uint64_t) * C::STAGES;
+}
+
+template <int KV, int LAYOUT>
+int prepare_kernel(int device) {
+  static bool done[64] = {};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (device < 0 || device >= 64) return fail(FK_ERR_INVALID_ARG, "device index %d out of range", device);
+  if (!done[device]) {
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_bytes<KV>()));
+    if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done[device] = true;
+  }
+  return FK_OK;
+}
+
+// Resident CTAs of the split kernel on `device` for KV type `kv`: the
+// persistent grid size S.  It depends on the KV type only (the three layout
+// instantiations share the shared-memory footprint and launch bounds), so
+// paged and contiguous calls plan identical segments.
+int num_work_ctas(int device, int kv) {
+  static int cache[64][3] = {};
+  static std::mutex mu;
+  if (device < 0 || device >= 64 || kv < 0 || kv > 2) return 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (cache[device][kv] > 0) return cache[device][kv];
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  int per_sm = 0;
+  cudaError_t e = cudaSuccess;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  switch (kv) {
+    case FK_DTYPE_F16:
+      if (prepare_kernel<FK_DTYPE_F16, VARLEN>(device) != FK_OK) break;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<FK_DTYPE_F16, VARLEN>, THREADS,
+                                                        smem_bytes<FK_DTYPE_F16>());
+      break;
+    case FK_DTYPE_BF16:
+      if (prepare_kernel<FK_DTYPE_BF16, VARLEN>(device) != FK_OK) break;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<FK_DTYPE_BF16, VARLEN>,
+                                                        THREADS, smem_bytes<FK_DTYPE_BF16>());
+      break;
+    default:
+      if (prepare_kernel<FK_DTYPE_E4M3, VARLEN>(device) != FK_OK) break;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<FK_DTYPE_E4M3, VARLEN>,
+                                                        THREADS, smem_bytes<FK_DTYPE_E4M3>());
+      break;
+  }
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess || per_sm <= 0) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  cache[device][kv] = sms * per_sm;
+  return cache[device][kv];
+}
+
+int encode_map(CUtensorMap* map, int kv, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_b,
+               const uint32_t* box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(FK_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t gd[5];
+  cuuint64_t gs[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_b[i];
+  const CUtensorMapDataType dt = (kv == FK_DTYPE_E4M3)   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : (kv == FK_DTYPE_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FK_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return FK_OK;
+}
+
+bool is16(int dt) { return dt == FK_DTYPE_F16 || dt == FK_DTYPE_BF16; }
+
+int common_checks(const void* q, const void* k, const void* v, const void* out, int batch, int q_heads, int kv_heads,
+                  int head_dim, int q_dtype, int kv_dtype, int out_dtype, void* ws, int* device) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(FK_ERR_INVALID_ARG, "q, k, v and out must be non-null");
+  if (ws == nullptr) return fail(FK_ERR_WORKSPACE, "workspace must be non-null");
+  if (batch < 0 || q_heads <= 0 || kv_heads <= 0)
+    return fail(FK_ERR_INVALID_ARG, "bad sizes: batch=%d q_heads=%d kv_heads=%d", batch, q_heads, kv_heads);
+  if (head_dim != HEAD_DIM) return fail(FK_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (q_heads % kv_heads != 0)
+    return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a multiple of kv_heads (%d)", q_heads, kv_heads);
+  if (q_heads / kv_heads > GPAD)
+    return fail(FK_ERR_UNSUPPORTED, "GQA group size %d > %d is not supported", q_heads / kv_heads, GPAD);
+  if (!is16(out_dtype)) return fail(FK_ERR_UNSUPPORTED, "out dtype must be f16 or bf16");
+  if (kv_dtype != FK_DTYPE_E4M3 && !is16(kv_dtype)) return fail(FK_ERR_UNSUPPORTED, "unsupported kv dtype %d", kv_dtype);
+  if (q_dtype != FK_DTYPE_E4M3 && !is16(q_dtype)) return fail(FK_ERR_UNSUPPORTED, "unsupported q dtype %d", q_dtype);
+  if (is16(kv_dtype) && q_dtype != kv_dtype)
+    return fail(FK_ERR_INVALID_ARG, "q dtype must equal the 16-bit kv dtype");
+  const int es = (kv_dtype == FK_DTYPE_E4M3) ? 1 : 2;
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15)
+    return fail(FK_ERR_INVALID_ARG, "k/v base addresses must be 16-byte aligned");
+  (void)es;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, k) != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return fail(FK_ERR_INVALID_ARG, "k must be device memory");
+  }
+  *device = attr.device;
+  return FK_OK;
+}
+
+template <int LAYOUT>
+int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) {
+  const int S = num_work_ctas(device, kv);
+  if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
+  p.num_ctas = S;
+  const WsLayout wl(p.B, p.kv_heads, S);
+  if (ws_bytes < wl.total)
+    return fail(FK_ERR_WORKSPACE, "workspace too small: %zu bytes < %zu required", ws_bytes, wl.total);
+  if (p.B == 0) return FK_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  int rc = FK_OK;
+  prof_mark(0, stream);
+  switch (kv) {
+    case FK_DTYPE_F16:
+      rc = prepare_kernel<FK_DTYPE_F16, LAYOUT>(device);
+      if (rc == FK_OK)
+        decode_split_kernel<FK_DTYPE_F16, LAYOUT><<<S, THREADS, smem_bytes<FK_DTYPE_F16>(), stream>>>(p);
+      break;
+    case FK_DTYPE_BF16:
+      rc = prepare_kernel<FK_DTYPE_BF16, LAYOUT>(device);
+      if (rc == FK_OK)
+        decode_split_kernel<FK_DTYPE_BF16, LAYOUT><<<S, THREADS, smem_bytes<FK_DTYPE_BF16>(), stream>>>(p);
+      break;
+    default:
+      rc = prepare_kernel<FK_DTYPE_E4M3, LAYOUT>(device);
+      if (rc == FK_OK)
+        decode_split_kernel<FK_DTYPE_E4M3, LAYOUT><<<S, THREADS, smem_bytes<FK_DTYPE_E4M3>(), stream>>>(p);
+      break;
+  }
+  if (rc == FK_OK) {
+    prof_mark(1, stream);
+    decode_combine_kernel<LAYOUT><<<p.B * p.kv_heads, 128, 0, stream>>>(p);
+    prof_mark(2, stream);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = fail(FK_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  }
+  if (prev != device) cudaSetDevice(prev);
+  return rc;
+}
+
+void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out, int64_t so_b, int64_t so_h,
+                 const float* s_aux, int batch, int q_heads, int kv_heads, int q_dtype, int out_dtype,
+                 const float* scale_q, const float* scale_k, const float* scale_v, void* ws) {
+  p.q = q;
+  p.q_sb = sq_b;
+  p.q_sh = sq_h;
+  p.out = out;
+  p.o_sb = so_b;
+  p.o_sh = so_h;
+  p.s_aux = s_aux;
+  p.B = batch;
+  p.q_heads = q_heads;
+  p.kv_heads = kv_heads;
+  p.G = q_heads / kv_heads;
+  p.q_dtype = q_dtype;
+  p.out_dtype = out_dtype;
+  p.scale_q = scale_q;
+  p.scale_k = scale_k;
+  p.scale_v = scale_v;
+  p.ws = static_cast<unsigned char*>(ws);
+}
+
+}  // namespace fk
+
+// ==========================================================================
+// C ABI
+// ==========================================================================
+using namespace fk;
+
+extern "C" int fk_version(void) { return 100; }
+
+extern "C" const char* fk_last_error(void) { return g_err.c_str(); }
+
+extern "C" size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads, int kv_dtype) {
+  if (batch < 0 || kv_heads <= 0) {
+    fail(FK_ERR_INVALID_ARG, "bad sizes");
+    return 0;
+  }
+  const int S = num_work_ctas(device, kv_dtype);
+  if (S <= 0) {
+    fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
+    return 0;
+  }
+  return WsLayout(batch, kv_heads, S).total;
+}
+
+extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, const void* v_varlen,
+                                          const int32_t* cu_seqlens_k, const float* s_aux, void* out, int batch,
+                                          int q_heads, int kv_heads, int head_dim, int64_t total_tokens, int dtype,
+                                          int64_t sq_b, int64_t sq_h, int64_t sk_t, int64_t sk_h, int64_t sv_t,
+                                          int64_t sv_h, int64_t so_b, int64_t so_h, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  int device = 0;
+  int rc = common_checks(q, k_varlen, v_varlen, out, batch, q_heads, kv_heads, head_dim, dtype, dtype, dtype,
+                         workspace, &device);
+  if (rc != FK_OK) return rc;
+  if (!is16(dtype)) return fail(FK_ERR_UNSUPPORTED, "varlen decode takes f16 or bf16 tensors");
+  if (cu_seqlens_k == nullptr) return fail(FK_ERR_INVALID_ARG, "cu_seqlens_k must be non-null");
+  if (total_tokens < 0 || total_tokens > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad total_tokens");
+  if (((sk_t | sk_h | sv_t | sv_h) * 2) % 16 != 0)
+    return fail(FK_ERR_INVALID_ARG, "k/v strides must be multiples of 16 bytes");
+  Params p;
+  memset(&p, 0, sizeof(p));
+  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, dtype, dtype, nullptr, nullptr,
+              nullptr, workspace);
+  p.lens = cu_seqlens_k;
+  const uint64_t T = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
+  const uint64_t dims[3] = {HEAD_DIM, static_cast<uint64_t>(kv_heads), T};
+  const uint32_t box[3] = {64, 1, TILE};
+  const uint64_t ks[2] = {static_cast<uint64_t>(sk_h) * 2, static_cast<uint64_t>(sk_t) * 2};
+  const uint64_t vs[2] = {static_cast<uint64_t>(sv_h) * 2, static_cast<uint64_t>(sv_t) * 2};
+  if ((rc = encode_map(&p.tk, dtype, 3, k_varlen, dims, ks, box)) != FK_OK) return rc;
+  if ((rc = encode_map(&p.tv, dtype, 3, v_varlen, dims, vs, box)) != FK_OK) return rc;
+  return launch<VARLEN>(p, dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, const void* v_cache,
+                                            const int32_t* cache_lens, const int32_t* start_k_offsets,
+                                            const float* s_aux, void* out, int batch, int q_heads, int kv_heads,
+                                            int head_dim, int64_t max_seqlen, int q_dtype, int kv_dtype,
+                                            int out_dtype, const float* scale_q, const float* scale_k,
+                                            const float* scale_v, int64_t sq_b, int64_t sq_h, int64_t sk_b,
+                                            int64_t sk_h, int64_t sk_s, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                                            int64_t so_b, int64_t so_h, void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+  int device = 0;
+  int rc = common_checks(q, k_cache, v_cache, out, batch, q_heads, kv_heads, head_dim, q_dtype, kv_dtype, out_dtype,
+                         workspace, &device);
+  if (rc != FK_OK) return rc;
+  if (cache_lens == nullptr) return fail(FK_ERR_INVALID_ARG, "cache_lens must be non-null");
+  if (max_seqlen <= 0 || max_seqlen > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad max_seqlen");
+  const int es = (kv_dtype == FK_DTYPE_E4M3) ? 1 : 2;
+  if (((sk_b | sk_h | sk_s | sv_b | sv_h | sv_s) * es) % 16 != 0)
+    return fail(FK_ERR_INVALID_ARG, "k/v cache strides must be multiples of 16 bytes");
+  Params p;
+  memset(&p, 0, sizeof(p));
+  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, q_dtype, out_dtype, scale_q,
+              scale_k, scale_v, workspace);
+  p.lens = cache_lens;
+  p.starts = start_k_offsets;
+  p.max_tokens = max_seqlen;
+  const uint32_t bd = (kv_dtype == FK_DTYPE_E4M3) ? 128 : 64;
+  const uint64_t dims[4] = {HEAD_DIM, static_cast<uint64_t>(max_seqlen), static_cast<uint64_t>(kv_heads),
+                            static_cast<uint64_t>(batch > 0 ? batch : 1)};
+  const uint32_t box[4] = {bd, TILE, 1, 1};
+  const uint64_t ks[3] = {static_cast<uint64_t>(sk_s) * es, static_cast<uint64_t>(sk_h) * es,
+                          static_cast<uint64_t>(sk_b) * es};
+  const uint64_t vs[3] = {static_cast<uint64_t>(sv_s) * es, static_cast<uint64_t>(sv_h) * es,
+                          static_cast<uint64_t>(sv_b) * es};
+  if ((rc = encode_map(&p.tk, kv_dtype, 4, k_cache, dims, ks, box)) != FK_OK) return rc;
+  if ((rc = encode_map(&p.tv, kv_dtype, 4, v_cache, dims, vs, box)) != FK_OK) return rc;
+  return launch<DENSE>(p, kv_dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const void* v_pool,
+                                     const int32_t* block_table, const int32_t* seq_lens, const float* s_aux,
+                                     void* out, int batch, int q_heads, int kv_heads, int head_dim,
+                                     int64_t num_pages, int page_size, int max_blocks, int q_dtype, int kv_dtype,
+                                     int out_dtype, const float* scale_q, const float* scale_k,
+                                     const float* scale_v, int64_t sq_b, int64_t sq_h, int64_t sk_p, int64_t sk_h,
+                                     int64_t sk_s, int64_t sv_p, int64_t sv_h, int64_t sv_s, int64_t bt_b,
+                                     int64_t so_b, int64_t so_h, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  int device = 0;
+  int rc = common_checks(q, k_pool, v_pool, out, batch, q_heads, kv_heads, head_dim, q_dtype, kv_dtype, out_dtype,
+                         workspace, &device);
+  if (rc != FK_OK) return rc;
+  if (page_size != PAGE) return fail(FK_ERR_UNSUPPORTED, "page_size must be 16 (got %d)", page_size);
+  if (block_table == nullptr || seq_lens == nullptr)
+    return fail(FK_ERR_INVALID_ARG, "block_table and seq_lens must be non-null");
+  if (num_pages <= 0 || num_pages > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad num_pages");
+  if (max_blocks < 0) return fail(FK_ERR_INVALID_ARG, "bad max_blocks");
+  const int es = (kv_dtype == FK_DTYPE_E4M3) ? 1 : 2;
+  if (((sk_p | sk_h | sk_s | sv_p | sv_h | sv_s) * es) % 16 != 0)
+    return fail(FK_ERR_INVALID_ARG, "k/v pool strides must be multiples of 16 bytes");
+  Params p;
+  memset(&p, 0, sizeof(p));
+  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, q_dtype, out_dtype, scale_q,
+              scale_k, scale_v, workspace);
+  p.lens = seq_lens;
+  p.bt = block_table;
+  p.bt_sb = bt_b;
+  p.max_blocks = max_blocks;
+  p.num_pages = static_cast<int>(num_pages);
+  const uint32_t bd = (kv_dtype == FK_DTYPE_E4M3) ? 128 : 64;
+  const uint64_t dims[4] = {HEAD_DIM, PAGE, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
+  const uint32_t box[4] = {bd, PAGE, 1, 1};
+  const uint64_t ks[3] = {static_cast<uint64_t>(sk_s) * es, static_cast<uint64_t>(sk_h) * es,
+                          static_cast<uint64_t>(sk_p) * es};
+  const uint64_t vs[3] = {static_cast<uint64_t>(sv_s) * es, static_cast<uint64_t>(sv_h) * es,
+                          static_cast<uint64_t>(sv_p) * es};
+  if ((rc = encode_map(&p.tk, kv_dtype, 4, k_pool, dims, ks, box)) != FK_OK) return rc;
+  if ((rc = encode_map(&p.tv, kv_dtype, 4, v_pool, dims, vs, box)) != FK_OK) return rc;
+  return launch<PAGED>(p, kv_dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fk_profile_begin(int max_launches) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  if (max_launches <= 0) return fail(FK_ERR_INVALID_ARG, "max_launches must be positive");
+  if (g_prof.ev != nullptr) {
+    for (int i = 0; i < 3 * g_prof.cap; ++i) cudaEventDestroy(g_prof.ev[i]);
+    delete[] g_prof.ev;
+  }
+  g_prof.ev = new cudaEvent_t[3 * max_launches];
+  for (int i = 0; i < 3 * max_launches; ++i) {
+    const cudaError_t e = cudaEventCreate(&g_prof.ev[i]);
+    if (e != cudaSuccess) {
+      g_prof.cap = i / 3;
+      g_prof.on = false;
+      return fail(FK_ERR_CUDA, "cudaEventCreate: %s", cudaGetErrorString(e));
+    }
+  }
+  g_prof.cap = max_launches;
+  g_prof.n = 0;
+  g_prof.on = true;
+  return FK_OK;
+}
+
+extern "C" int fk_profile_end(float* split_ms, float* combine_ms, int* launches) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.on = false;
+  float s = 0.f, c = 0.f;
+  for (int i = 0; i < g_prof.n; ++i) {
+    float a = 0.f, b = 0.f;
+    if (cudaEventSynchronize(g_prof.ev[3 * i + 2]) != cudaSuccess) return fail(FK_ERR_CUDA, "event sync failed");
+    cudaEventElapsedTime(&a, g_prof.ev[3 * i], g_prof.ev[3 * i + 1]);
+    cudaEventElapsedTime(&b, g_prof.ev[3 * i + 1], g_prof.ev[3 * i + 2]);
+    s += a;
+    c += b;
+  }
+  if (split_ms) *split_ms = s;
+  if (combine_ms) *combine_ms = c;
+  if (launches) *launches = g_prof.n;
+  return FK_OK;
+}
+
+extern "C" int fk_decode_num_ctas(int device, int kv_dtype) { return num_work_ctas(device, kv_dtype); }

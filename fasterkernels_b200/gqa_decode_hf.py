@@ -1,0 +1,146 @@
+"""HF dense-cache GQA decode and the Hugging Face attention adapter.
+
+Drop-in for fskernels/triton/triton_gqa_decode_hf.py:
+  * ``set_num_splits`` (:12-14) -- kept for CUDAGraphRunner
+    (fskernels/engine/cuda_graph_runner.py:175-176).  The split count here is
+    planned on the device from the sequence lengths, so the value is recorded
+    (``get_num_splits``) and accepted but does not change the result or the
+    schedule.
+  * ``flash_decode_gqa_hf_dense_optimized(q, k_cache, v_cache, cache_lens,
+    start_k_offsets=None, num_splits=None)`` (:146-211): sequence b attends
+    cache rows start_k_offsets[b] .. cache_lens[b]-1 (:44-50).  Partials are
+    kept in fp32 (the reference stores them in the output dtype, :182).
+  * ``custom_hf_decode_attention_forward`` (:218-258): q_len == 1 with a cache
+    and ``cache_position`` -> the sm_100a kernel; anything else -> the
+    transformers eager attention, exactly as the reference routes prefill.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _native as N
+from .gqa_decode import HEAD_DIM, _check_idx, _check_sink, _inner_contig
+
+_DECODE_NUM_SPLITS: int = 1
+
+
+def set_num_splits(n: int) -> None:
+    global _DECODE_NUM_SPLITS
+    n = int(n)
+    if n < 1:
+        raise ValueError("num_splits must be >= 1")
+    _DECODE_NUM_SPLITS = n
+
+
+def get_num_splits() -> int:
+    return _DECODE_NUM_SPLITS
+
+
+def _scale_ptr(x, dev):
+    if x is None:
+        return None
+    if not torch.is_tensor(x):
+        x = torch.tensor(float(x), dtype=torch.float32, device=dev)
+    if x.device != dev:
+        raise ValueError("FP8 scales must be device tensors on q's device")
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        x = x.reshape(()).to(torch.float32).contiguous()
+    return x
+
+
+def dense_decode(q, k_cache, v_cache, cache_lens, start_k_offsets=None, *, s_aux=None, scale_q=None,
+                 scale_k=None, scale_v=None, out_dtype=None, out=None):
+    """Core HF-dense entry: k/v [B, KV_H, S, 128] in float16/bfloat16 (q the same
+    dtype) or float8_e4m3fn (q float16/bfloat16, or float8_e4m3fn with scale_q)."""
+    if q.dim() != 3 or k_cache.dim() != 4 or v_cache.dim() != 4:
+        raise ValueError("q must be [B, Q_H, D] and k/v caches [B, KV_H, S, D]")
+    if not q.is_cuda:
+        raise ValueError("dense decode runs on CUDA tensors only")
+    dev = q.device
+    if k_cache.device != dev or v_cache.device != dev:
+        raise ValueError("q and the caches must be on the same device")
+    if k_cache.dtype != v_cache.dtype or k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache must match in shape and dtype")
+    B, QH, D = q.shape
+    Bk, KVH, S, D2 = k_cache.shape
+    if D != HEAD_DIM or D2 != HEAD_DIM:
+        raise ValueError(f"head_dim must be {HEAD_DIM}")
+    if Bk < B:
+        raise ValueError("cache batch is smaller than q's batch")
+    kv_code = N.dtype_code(k_cache.dtype)
+    q_code = N.dtype_code(q.dtype)
+    if out_dtype is None:
+        out_dtype = q.dtype if q.dtype != torch.float8_e4m3fn else torch.float16
+    out_code = N.dtype_code(out_dtype)
+    q = _inner_contig(q, "q")
+    k_cache = _inner_contig(k_cache, "k_cache")
+    v_cache = _inner_contig(v_cache, "v_cache")
+    lens = _check_idx(cache_lens, "cache_lens", dev)
+    if lens.numel() < B:
+        raise ValueError("cache_lens must have one entry per sequence")
+    starts = None if start_k_offsets is None else _check_idx(start_k_offsets, "start_k_offsets", dev)
+    s_aux = _check_sink(s_aux, QH, dev)
+    sq = _scale_ptr(scale_q, dev) if q.dtype == torch.float8_e4m3fn else None
+    sk = _scale_ptr(scale_k, dev) if kv_code == N.FK_DTYPE_E4M3 else None
+    sv = _scale_ptr(scale_v, dev) if kv_code == N.FK_DTYPE_E4M3 else None
+    if out is None:
+        out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
+    elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
+        raise ValueError("out must be [B, Q_H, 128] of out_dtype with unit inner stride")
+    ws = N.workspace(dev, B, KVH, kv_code)
+    rc = N.lib().fk_flash_decode_gqa_hf_dense(
+        N.ptr(q), N.ptr(k_cache), N.ptr(v_cache), N.ptr(lens), N.ptr(starts), N.ptr(s_aux), N.ptr(out),
+        B, QH, KVH, D, S, q_code, kv_code, out_code, N.ptr(sq), N.ptr(sk), N.ptr(sv),
+        q.stride(0), q.stride(1), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+        v_cache.stride(0), v_cache.stride(1), v_cache.stride(2), out.stride(0), out.stride(1),
+        N.ptr(ws), ws.numel(), N.stream_of(dev))
+    N.check(rc, "fk_flash_decode_gqa_hf_dense")
+    return out
+
+
+def flash_decode_gqa_hf_dense_optimized(q, k_cache, v_cache, cache_lens, start_k_offsets=None, num_splits=None,
+                                        *, s_aux=None, out=None):
+    """Decode over an HF BHSD cache.  ``num_splits`` is accepted for API
+    compatibility; the split schedule is planned on the device."""
+    if num_splits is not None and int(num_splits) < 1:
+        raise ValueError("num_splits must be >= 1")
+    if q.dtype not in (torch.float16, torch.bfloat16) or k_cache.dtype != q.dtype:
+        raise TypeError("flash_decode_gqa_hf_dense_optimized takes float16/bfloat16 q and caches of q's dtype")
+    return dense_decode(q, k_cache, v_cache, cache_lens, start_k_offsets, s_aux=s_aux, out=out)
+
+
+def _module_sinks(module, q_heads, dev):
+    sinks = getattr(module, "sinks", None)
+    if sinks is None or not torch.is_tensor(sinks) or sinks.numel() != q_heads:
+        return None
+    return sinks.detach().to(device=dev, dtype=torch.float32).reshape(-1)
+
+
+def _decode_window(kwargs, bsz, dev):
+    """cache_lens (and the sliding-window start) from ``cache_position``, with
+    tensor ops only (graph-safe), as triton_gqa_decode_hf.py:239-250 does.
+    The window is [max(0, len - window), len)."""
+    cache_position = kwargs.get("cache_position")
+    lens = (cache_position[-1:] + 1).to(torch.int32).expand(bsz).contiguous()
+    window = kwargs.get("sliding_window")
+    starts = None
+    if window is not None:
+        starts = torch.clamp(lens - int(window), min=0).to(torch.int32)
+    return lens, starts
+
+
+def custom_hf_decode_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling: float,
+                                       dropout: float = 0.0, **kwargs) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    bsz, q_heads, q_len, head_dim = query_states.shape
+    if (kwargs.get("past_key_values") is not None and q_len == 1 and kwargs.get("cache_position") is not None
+            and query_states.is_cuda and head_dim == HEAD_DIM):
+        q = query_states.squeeze(2)
+        lens, starts = _decode_window(kwargs, bsz, q.device)
+        out = dense_decode(q, key_states, value_states, lens, starts,
+                           s_aux=_module_sinks(module, q_heads, q.device))
+        return out, None
+    from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
+    return eager_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling, dropout,
+                                   **kwargs)

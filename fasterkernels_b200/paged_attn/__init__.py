@@ -1,0 +1,5 @@
+"""Paged KV cache and paged decode (mirrors fskernels/paged_attn/__init__.py:1-4)."""
+from .paged_decode import paged_flash_decode
+from .paged_kv_cache import PAGE_SIZE, PagedKVCache
+
+__all__ = ["PagedKVCache", "PAGE_SIZE", "paged_flash_decode"]

@@ -1,0 +1,117 @@
+"""Host-side page allocator for a paged KV cache.
+
+Same contract as the reference's ``PagedKVCache`` and ``PAGE_SIZE``
+(fskernels/paged_attn/paged_kv_cache.py:6-154): pools
+[num_layers, num_pages, num_kv_heads, 16, head_dim], a device block table
+[max_seqs, max_blocks_per_seq] int32 with -1 for unallocated entries, a free
+list, ``allocate_sequence``/``free_sequence``/``append_kv``/
+``get_block_table_tensor``/``get_seq_lens_tensor`` and the
+``pages_used``/``pages_free`` counters.
+
+Differences: the logical->physical map is mirrored on the host, so neither
+``append_kv`` nor ``free_sequence`` reads the device block table back (the
+reference calls ``.item()`` per appended token, paged_kv_cache.py:126);
+``from_config`` honours a ``dtype`` argument (the reference hard-wires
+bfloat16, :80); pools may be float8_e4m3fn.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List
+
+import torch
+
+PAGE_SIZE = 16
+
+
+@dataclass
+class PagedKVCache:
+    num_layers: int
+    num_pages: int
+    max_seqs: int
+    max_blocks_per_seq: int
+    num_kv_heads: int
+    head_dim: int
+    dtype: torch.dtype
+    device: str
+
+    def __post_init__(self):
+        shape = (self.num_layers, self.num_pages, self.num_kv_heads, PAGE_SIZE, self.head_dim)
+        self.k_pool = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        self.v_pool = torch.zeros_like(self.k_pool)
+        self.block_table = torch.full((self.max_seqs, self.max_blocks_per_seq), -1, dtype=torch.int32,
+                                      device=self.device)
+        self._seq_lens: List[int] = [0] * self.max_seqs
+        self._active: List[bool] = [False] * self.max_seqs
+        self._pages: List[List[int]] = [[] for _ in range(self.max_seqs)]
+        # popped from the end: lowest page indices are handed out last, as in the reference
+        self._free_pages: List[int] = list(range(self.num_pages))
+
+    @classmethod
+    def from_config(cls, config, num_pages: int = 4096, max_seqs: int = 16, max_blocks_per_seq: int = 512,
+                    device: str = "cuda", dtype: torch.dtype = torch.bfloat16) -> "PagedKVCache":
+        head_dim = getattr(config, "head_dim", None) or config.hidden_size // config.num_attention_heads
+        return cls(num_layers=config.num_hidden_layers, num_pages=num_pages, max_seqs=max_seqs,
+                   max_blocks_per_seq=max_blocks_per_seq, num_kv_heads=config.num_key_value_heads,
+                   head_dim=head_dim, dtype=dtype, device=device)
+
+    def allocate_sequence(self) -> int:
+        for sid in range(self.max_seqs):
+            if not self._active[sid]:
+                self._active[sid] = True
+                self._seq_lens[sid] = 0
+                self._pages[sid] = []
+                return sid
+        raise RuntimeError("All sequence slots are occupied")
+
+    def free_sequence(self, seq_id: int) -> None:
+        pages = self._pages[seq_id]
+        if pages:
+            self.block_table[seq_id, : len(pages)] = -1
+            self._free_pages.extend(pages)
+        self._pages[seq_id] = []
+        self._active[seq_id] = False
+        self._seq_lens[seq_id] = 0
+
+    def _alloc_page(self) -> int:
+        if not self._free_pages:
+            raise RuntimeError("Out of KV pages")
+        return self._free_pages.pop()
+
+    def append_kv(self, seq_id: int, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Append one token's K/V ([1, KV_H, 1, D]) to a sequence of one layer."""
+        pos = self._seq_lens[seq_id]
+        page_idx, off = divmod(pos, PAGE_SIZE)
+        pages = self._pages[seq_id]
+        if page_idx == len(pages):
+            if page_idx >= self.max_blocks_per_seq:
+                raise RuntimeError("sequence exceeds max_blocks_per_seq")
+            pp = self._alloc_page()
+            pages.append(pp)
+            self.block_table[seq_id, page_idx] = pp
+        pp = pages[page_idx]
+        self.k_pool[layer_idx, pp, :, off, :] = k[0, :, 0, :]
+        self.v_pool[layer_idx, pp, :, off, :] = v[0, :, 0, :]
+        self._seq_lens[seq_id] = pos + 1
+
+    def seq_len(self, seq_id: int) -> int:
+        return self._seq_lens[seq_id]
+
+    def get_block_table_tensor(self, active_seq_ids: List[int]) -> torch.Tensor:
+        idx = torch.tensor(active_seq_ids, dtype=torch.long, device=self.device)
+        return self.block_table[idx]
+
+    def get_seq_lens_tensor(self, active_seq_ids: List[int]) -> torch.Tensor:
+        return torch.tensor([self._seq_lens[s] for s in active_seq_ids], dtype=torch.int32, device=self.device)
+
+    @property
+    def pages_used(self) -> int:
+        return self.num_pages - len(self._free_pages)
+
+    @property
+    def pages_free(self) -> int:
+        return len(self._free_pages)
+
+    def __repr__(self) -> str:
+        return (f"PagedKVCache(pages={self.num_pages}, used={self.pages_used}, "
+                f"seqs={sum(self._active)}/{self.max_seqs})")

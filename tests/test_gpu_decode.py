@@ -1,0 +1,277 @@
+"""GPU parity tests: the sm_100a kernels (through the C-ABI via the Python
+entry points) against the golden vectors and the CPU oracle.
+
+Tolerances: fp16 output atol 2e-3 / rtol 1e-2 (fp32 accumulation); bf16
+atol 1e-2 / rtol 2e-2 (bf16 P and V operands); FP8 KV atol 2e-2 against the
+oracle on the dequantised KV; paged vs contiguous bit-identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+import fasterkernels_b200 as fk
+from fasterkernels_b200 import _native as N
+from fasterkernels_b200 import workloads as W
+from oracle import gqa_decode_oracle as O
+from tests._golden import e4m3_to_float, load, varlen_cases
+
+pytestmark = pytest.mark.gpu
+F16_TOL = dict(atol=2e-3, rtol=1e-2)
+BF16_TOL = dict(atol=1e-2, rtol=2e-2)
+FP8_TOL = dict(atol=2e-2, rtol=0)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    return torch.device("cuda", 0)
+
+
+def t(x, dev, dtype=None):
+    x = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    return x if dtype is None else x.to(dtype)
+
+
+def close(out, ref, **tol):
+    np.testing.assert_allclose(out.float().cpu().numpy(), np.asarray(ref, dtype=np.float64), **tol)
+
+
+# ------------------------------------------------------------- golden cases
+@pytest.mark.parametrize("name", varlen_cases())
+def test_varlen_golden(dev, name):
+    z = load(name)
+    s = None if "s_aux" not in z else t(z["s_aux"], dev)
+    out = fk.flash_decode_gqa_varlen(t(z["q"], dev), t(z["k"], dev), t(z["v"], dev), t(z["cu_seqlens"], dev), s)
+    torch.cuda.synchronize()
+    close(out, z["ref"], **F16_TOL)
+    assert N.read_status(dev) == 0
+
+
+def test_paged_golden_and_bit_identity(dev):
+    z = load("paged_g4")
+    q = t(z["q"], dev)
+    kp, vp, bt, sl = t(z["k_pool"], dev), t(z["v_pool"], dev), t(z["block_table"], dev), t(z["seq_lens"], dev)
+    out = fk.paged_flash_decode(q, kp, vp, bt, sl, 16)
+    close(out, z["ref"], **F16_TOL)
+    # same logical KV laid out contiguously -> bit-identical output
+    lens = z["seq_lens"].tolist()
+    ks = O.paged_to_dense(z["k_pool"], z["block_table"], z["seq_lens"])
+    vs = O.paged_to_dense(z["v_pool"], z["block_table"], z["seq_lens"])
+    kv = np.concatenate([x.transpose(1, 0, 2) for x in ks], 0)
+    vv = np.concatenate([x.transpose(1, 0, 2) for x in vs], 0)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    out2 = fk.flash_decode_gqa_varlen(q, t(kv, dev), t(vv, dev), t(cu, dev))
+    assert torch.equal(out, out2)
+
+
+def test_dense_window_golden(dev):
+    z = load("dense_g4_window")
+    out = fk.flash_decode_gqa_hf_dense_optimized(t(z["q"], dev), t(z["k_cache"], dev), t(z["v_cache"], dev),
+                                                 t(z["cache_lens"], dev), t(z["start_k_offsets"], dev))
+    close(out, z["ref"], **F16_TOL)
+
+
+def test_fp8_golden(dev):
+    z = load("fp8_g4")
+    k8 = t(z["k_fp8"], dev).view(torch.float8_e4m3fn)
+    v8 = t(z["v_fp8"], dev).view(torch.float8_e4m3fn)
+    sk = torch.tensor(float(z["scale_k"]), device=dev)
+    sv = torch.tensor(float(z["scale_v"]), device=dev)
+    lens = t(z["cache_lens"], dev)
+    out = fk.flash_decode_gqa_hf_fp8(t(z["q"], dev), k8, v8, lens, None, sk, sv, torch.float16)
+    close(out, z["ref"], **FP8_TOL)
+    close(out, z["ref"], atol=3e-3, rtol=1e-2)  # fp16 Q, exact e4m3 widening: much tighter in practice
+    q8 = t(z["q_fp8"], dev).view(torch.float8_e4m3fn)
+    sq = torch.tensor(float(z["scale_q"]), device=dev)
+    out8 = fk.flash_decode_gqa_hf_fp8(q8, k8, v8, lens, sq, sk, sv, torch.float16)
+    close(out8, z["ref_q8"], **FP8_TOL)
+    close(out8, z["ref_kernel"], **FP8_TOL)
+
+
+# ------------------------------------------------------------- random cases
+def _rand_case(dev, lens, qh, kvh, dtype, sinks, seed):
+    d = W.make_varlen(lens, qh, kvh, torch.float32, dev, seed=seed, sinks=sinks)
+    q, k, v = d["q"].to(dtype), d["k"].to(dtype), d["v"].to(dtype)
+    return q, k, v, d["cu_seqlens"], d["s_aux"]
+
+
+def _oracle(q, k, v, cu, s):
+    return O.decode_varlen(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                           cu.cpu().numpy(), None if s is None else s.cpu().numpy())
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+@pytest.mark.parametrize("sinks", [False, True])
+def test_varlen_group_sizes(dev, G, sinks):
+    lens = [1, 15, 16, 17, 63, 64, 65, 700, 0, 2049]
+    q, k, v, cu, s = _rand_case(dev, lens, 4 * G, 4, torch.float16, sinks, seed=10 + G)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(out, _oracle(q, k, v, cu, s), **F16_TOL)
+
+
+def test_varlen_bf16(dev):
+    q, k, v, cu, s = _rand_case(dev, [5, 300, 4097, 33], 32, 8, torch.bfloat16, True, seed=3)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    assert out.dtype == torch.bfloat16
+    close(out, _oracle(q, k, v, cu, s), **BF16_TOL)
+
+
+def test_long_single_sequence_spans_many_ctas(dev):
+    # one sequence over every CTA: exercises the multi-segment combine
+    q, k, v, cu, s = _rand_case(dev, [70001], 32, 8, torch.float16, True, seed=4)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(out, _oracle(q, k, v, cu, s), **F16_TOL)
+
+
+def test_many_short_sequences(dev):
+    lens = [int(x) for x in torch.randint(0, 40, (700,), generator=torch.Generator().manual_seed(5))]
+    q, k, v, cu, s = _rand_case(dev, lens, 16, 4, torch.float16, True, seed=5)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(out, _oracle(q, k, v, cu, s), **F16_TOL)
+
+
+def test_empty_batch(dev):
+    q = torch.empty(0, 32, 128, device=dev, dtype=torch.float16)
+    k = torch.zeros(16, 8, 128, device=dev, dtype=torch.float16)
+    cu = torch.zeros(1, device=dev, dtype=torch.int32)
+    assert fk.flash_decode_gqa_varlen(q, k, k, cu).shape == (0, 32, 128)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_paged_random_bit_identical_to_varlen(dev, dtype):
+    lens = [1, 16, 17, 250, 3000, 0, 64, 1023]
+    q, k, v, cu, s = _rand_case(dev, lens, 32, 8, dtype, True, seed=6)
+    kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.25, seed=6)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    outp = fk.paged_flash_decode(q, kp, vp, bt, sl, 16, s_aux=s)
+    outv = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    assert torch.equal(outp, outv)
+    close(outp, _oracle(q, k, v, cu, s), **(F16_TOL if dtype == torch.float16 else BF16_TOL))
+
+
+def test_dense_bit_identical_to_varlen(dev):
+    lens = [100, 2000, 1]
+    S = 2100
+    q, k, v, cu, s = _rand_case(dev, lens, 32, 8, torch.float16, True, seed=7)
+    kc = torch.zeros(3, 8, S, 128, device=dev, dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    for b, L in enumerate(lens):
+        kc[b, :, :L] = k[cu[b]:cu[b + 1]].transpose(0, 1)
+        vc[b, :, :L] = v[cu[b]:cu[b + 1]].transpose(0, 1)
+    outd = fk.gqa_decode_hf.dense_decode(q, kc, vc, torch.tensor(lens, device=dev, dtype=torch.int32), s_aux=s)
+    outv = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    assert torch.equal(outd, outv)
+
+
+def test_fp8_paged_sinks_vs_dense_and_oracle(dev):
+    lens = [4000, 17, 1000, 2500]
+    d = W.make_varlen(lens, 64, 8, torch.float32, dev, seed=8, sinks=True)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    q = d["q"].half()
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=8)
+    kp, vp = kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    outp = fk.paged_flash_decode(q, kp, vp, bt, sl, 16, s_aux=d["s_aux"], scale_k=sk, scale_v=sv)
+    kd = (k8.float() * sk).cpu().numpy()
+    vd = (v8.float() * sv).cpu().numpy()
+    ref = O.decode_varlen(q.float().cpu().numpy(), kd, vd, d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
+    close(outp, ref, **FP8_TOL)
+    close(outp, ref, atol=3e-3, rtol=1e-2)
+    # dense cache with the same bytes -> bit-identical
+    S = max(lens)
+    kc = torch.zeros(4, 8, S, 128, device=dev, dtype=torch.uint8)
+    vc = torch.zeros_like(kc)
+    cu = d["cu_seqlens"]
+    for b, L in enumerate(lens):
+        kc[b, :, :L] = k8.view(torch.uint8)[cu[b]:cu[b + 1]].transpose(0, 1)
+        vc[b, :, :L] = v8.view(torch.uint8)[cu[b]:cu[b + 1]].transpose(0, 1)
+    outd = fk.flash_decode_gqa_hf_fp8(q, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), sl, None, sk,
+                                      sv, torch.float16, s_aux=d["s_aux"])
+    assert torch.equal(outd, outp)
+
+
+def test_bad_page_sets_status_and_masks(dev):
+    lens = [40]
+    q, k, v, cu, s = _rand_case(dev, lens, 32, 8, torch.float16, False, seed=9)
+    kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.0, seed=9)
+    N.read_status(dev)
+    bt_bad = bt.clone()
+    bt_bad[0, 1] = 10_000_000  # out of the pool: page 1 (tokens 16..31) is skipped and masked
+    out = fk.paged_flash_decode(q, kp, vp, bt_bad, torch.tensor(lens, device=dev, dtype=torch.int32), 16)
+    torch.cuda.synchronize()
+    assert N.read_status(dev) & N.FK_STATUS_BAD_PAGE
+    keep = torch.cat([torch.arange(0, 16), torch.arange(32, 40)]).to(dev)
+    cu2 = torch.tensor([0, 24], device=dev, dtype=torch.int32)
+    ref = fk.flash_decode_gqa_varlen(q, k[keep].contiguous(), v[keep].contiguous(), cu2)
+    close(out, ref.float().cpu().numpy(), atol=1e-3, rtol=1e-3)
+
+
+def test_cuda_graph_capture_and_replay(dev):
+    lens = [300, 5000, 77]
+    q, k, v, cu, s = _rand_case(dev, lens, 32, 8, torch.float16, True, seed=11)
+    out = torch.empty_like(q)
+    fk.flash_decode_gqa_varlen(q, k, v, cu, s, out=out)  # warm-up sizes the workspace
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fk.flash_decode_gqa_varlen(q, k, v, cu, s, out=out)
+    q.copy_(torch.randn_like(q))
+    cu.copy_(torch.tensor([0, 200, 5100, 5377], dtype=torch.int32, device=dev))  # new lengths, same graph
+    g.replay()
+    torch.cuda.synchronize()
+    close(out, _oracle(q, k, v, cu, s), **F16_TOL)
+
+
+def test_hf_adapter(dev):
+    class M:
+        num_key_value_heads = 8
+    lens_pos = torch.tensor([900], device=dev)
+    B, S = 2, 1024
+    qs = torch.randn(B, 32, 1, 128, device=dev, dtype=torch.float16)
+    ks = torch.randn(B, 8, S, 128, device=dev, dtype=torch.float16)
+    vs = torch.randn(B, 8, S, 128, device=dev, dtype=torch.float16)
+    out, w = fk.custom_hf_decode_attention_forward(M(), qs, ks, vs, None, 128 ** -0.5, past_key_values=object(),
+                                                   cache_position=lens_pos)
+    assert w is None and out.shape == (B, 32, 128)
+    ref = O.decode_dense(qs.squeeze(2).float().cpu().numpy(), ks.float().cpu().numpy(), vs.float().cpu().numpy(),
+                         [901, 901])
+    close(out, ref, **F16_TOL)
+    out_w, _ = fk.custom_hf_decode_attention_forward(M(), qs, ks, vs, None, 128 ** -0.5, past_key_values=object(),
+                                                     cache_position=lens_pos, sliding_window=256)
+    ref_w = O.decode_dense(qs.squeeze(2).float().cpu().numpy(), ks.float().cpu().numpy(), vs.float().cpu().numpy(),
+                           [901, 901], [645, 645])
+    close(out_w, ref_w, **F16_TOL)
+
+
+# ------------------------------------------------- full BASELINE sizes
+def test_config2_full_size(dev):
+    lens = W.config_lengths(2)
+    assert sum(lens) == 377152
+    d = W.make_varlen(lens, 32, 8, torch.float16, dev, seed=0, sinks=True)
+    out = fk.flash_decode_gqa_varlen(d["q"], d["k"], d["v"], d["cu_seqlens"], d["s_aux"])
+    cu = d["cu_seqlens"].cpu().numpy()
+    for b in (0, 17, 31):  # spot-check whole sequences against the oracle
+        lo, hi = cu[b], cu[b + 1]
+        ref = O.decode_varlen(d["q"][b:b + 1].float().cpu().numpy(), d["k"][lo:hi].float().cpu().numpy(),
+                              d["v"][lo:hi].float().cpu().numpy(), np.array([0, hi - lo]), d["s_aux"].cpu().numpy())
+        close(out[b:b + 1], ref, **F16_TOL)
+    # determinism: same inputs -> identical bits
+    assert torch.equal(out, fk.flash_decode_gqa_varlen(d["q"], d["k"], d["v"], d["cu_seqlens"], d["s_aux"]))
+    assert N.read_status(dev) == 0
+
+
+def test_config3_full_size_paged_equals_varlen(dev):
+    lens = W.config_lengths(3)
+    d = W.make_varlen(lens, 32, 8, torch.float16, dev, seed=0, sinks=False)
+    kp, vp, bt = W.varlen_to_paged(d["k"], d["v"], lens, 1.25, seed=0)
+    assert kp.shape[0] == 21555
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    outp = fk.paged_flash_decode(d["q"], kp, vp, bt, sl, 16)
+    outv = fk.flash_decode_gqa_varlen(d["q"], d["k"], d["v"], d["cu_seqlens"])
+    assert torch.equal(outp, outv)
+    cu = d["cu_seqlens"].cpu().numpy()
+    for b in (0, 63):
+        lo, hi = cu[b], cu[b + 1]
+        ref = O.decode_varlen(d["q"][b:b + 1].float().cpu().numpy(), d["k"][lo:hi].float().cpu().numpy(),
+                              d["v"][lo:hi].float().cpu().numpy(), np.array([0, hi - lo]))
+        close(outp[b:b + 1], ref, **F16_TOL)

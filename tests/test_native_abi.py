@@ -1,0 +1,63 @@
+"""The C-ABI library loads on a machine without a GPU and exports every entry
+point include/*.h declares; argument validation needs no device."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from fasterkernels_b200 import _native as N
+from fasterkernels_b200.build import LIB_PATH, build_library
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names |= set(re.findall(r"\b(fk_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_library_builds_and_loads():
+    build_library()
+    assert os.path.exists(LIB_PATH)
+    assert N.lib().fk_version() == 100
+
+
+def test_every_declared_symbol_is_exported():
+    syms = declared_symbols()
+    assert {"fk_flash_decode_gqa_varlen", "fk_flash_decode_gqa_hf_dense", "fk_paged_flash_decode",
+            "fk_decode_workspace_bytes", "fk_last_error", "fk_version"} <= syms
+    L = ctypes.CDLL(LIB_PATH)
+    for s in sorted(syms):
+        assert hasattr(L, s), s
+
+
+def test_invalid_arguments_are_rejected_without_touching_the_device():
+    L = N.lib()
+    rc = L.fk_flash_decode_gqa_varlen(None, None, None, None, None, None, 1, 32, 8, 128, 16, 0,
+                                      0, 0, 0, 0, 0, 0, 0, 0, None, 0, None)
+    assert rc == 1 and "non-null" in N.last_error()
+    fake = ctypes.c_void_p(16)
+    rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 32, 8, 64, 16, 0,
+                                      0, 0, 0, 0, 0, 0, 0, 0, fake, 0, None)
+    assert rc == 2 and "head_dim" in N.last_error()
+    rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 96, 8, 128, 16, 0,
+                                      0, 0, 0, 0, 0, 0, 0, 0, fake, 0, None)
+    assert rc == 2 and "group size" in N.last_error()
+    rc = L.fk_paged_flash_decode(fake, fake, fake, fake, fake, None, fake, 1, 32, 8, 128, 10, 32, 4, 0, 0, 0,
+                                 None, None, None, *([0] * 11), fake, 0, None)
+    assert rc in (1, 2)
+
+
+def test_entry_points_reject_cpu_tensors():
+    import torch
+    import fasterkernels_b200 as fk
+    q = torch.zeros(1, 32, 128, dtype=torch.float16)
+    k = torch.zeros(4, 8, 128, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        fk.flash_decode_gqa_varlen(q, k, k, torch.tensor([0, 4], dtype=torch.int32))

@@ -1,0 +1,84 @@
+"""Host logic of PagedKVCache (CPU tensors): same contract as the reference's
+allocator (fskernels/paged_attn/paged_kv_cache.py:85-154)."""
+import pytest
+import torch
+
+from fasterkernels_b200.paged_attn import PAGE_SIZE, PagedKVCache
+from fasterkernels_b200 import workloads as W
+
+
+def make(pages=8, seqs=3, blocks=4):
+    return PagedKVCache(num_layers=2, num_pages=pages, max_seqs=seqs, max_blocks_per_seq=blocks, num_kv_heads=2,
+                        head_dim=128, dtype=torch.float16, device="cpu")
+
+
+def test_append_and_block_table():
+    c = make()
+    s = c.allocate_sequence()
+    toks = []
+    for i in range(PAGE_SIZE + 3):
+        k = torch.full((1, 2, 1, 128), float(i), dtype=torch.float16)
+        c.append_kv(s, 1, k, -k)
+        toks.append(i)
+    assert c.seq_len(s) == PAGE_SIZE + 3
+    bt = c.get_block_table_tensor([s])
+    assert bt.shape == (1, 4) and (bt[0, :2] >= 0).all() and (bt[0, 2:] == -1).all()
+    p1 = int(bt[0, 1])
+    assert float(c.k_pool[1, p1, 0, 2, 0]) == PAGE_SIZE + 2
+    assert float(c.v_pool[1, p1, 1, 2, 5]) == -(PAGE_SIZE + 2)
+    assert c.get_seq_lens_tensor([s]).tolist() == [PAGE_SIZE + 3]
+    assert c.pages_used == 2 and c.pages_free == 6
+
+
+def test_free_returns_pages_and_slots():
+    c = make()
+    a, b = c.allocate_sequence(), c.allocate_sequence()
+    for _ in range(40):
+        c.append_kv(a, 0, torch.zeros(1, 2, 1, 128, dtype=torch.float16), torch.zeros(1, 2, 1, 128, dtype=torch.float16))
+    assert c.pages_used == 3
+    c.free_sequence(a)
+    assert c.pages_used == 0 and (c.block_table[a] == -1).all()
+    assert c.allocate_sequence() == a
+    c.allocate_sequence()
+    with pytest.raises(RuntimeError, match="occupied"):
+        c.allocate_sequence()
+    assert "PagedKVCache" in repr(c)
+
+
+def test_out_of_pages():
+    c = make(pages=1)
+    s = c.allocate_sequence()
+    z = torch.zeros(1, 2, 1, 128, dtype=torch.float16)
+    for _ in range(PAGE_SIZE):
+        c.append_kv(s, 0, z, z)
+    with pytest.raises(RuntimeError, match="Out of KV pages"):
+        c.append_kv(s, 0, z, z)
+
+
+def test_varlen_to_paged_roundtrip_cpu():
+    lens = [1, 16, 17, 40]
+    d = W.make_varlen(lens, 8, 2, torch.float16, "cpu", seed=3, sinks=False)
+    kp, vp, bt = W.varlen_to_paged(d["k"], d["v"], lens, 1.25, seed=3)
+    cu = d["cu_seqlens"]
+    for b, L in enumerate(lens):
+        for tok in range(L):
+            p, o = divmod(tok, PAGE_SIZE)
+            assert torch.equal(kp[int(bt[b, p]), :, o], d["k"][cu[b] + tok])
+    assert len(set(bt[bt >= 0].tolist())) == sum((L + 15) // 16 for L in lens)
+
+
+def test_config_lengths_match_the_seed_protocol():
+    assert sum(W.config_lengths(2)) == 377152
+    l3 = W.config_lengths(3)
+    assert sum(l3) == 275479 and sum((L + 15) // 16 for L in l3) == 17244
+    assert W.config_lengths(4) == [32768] * 16
+    assert W.kv_bytes(W.config_lengths(2), 8, 2) == 1544814592
+
+
+def test_lpt_partition_balances():
+    lens = W.config_lengths(5)
+    for n in (2, 4, 8):
+        parts = W.lpt_partition(lens, n)
+        assert sorted(i for p in parts for i in p) == list(range(len(lens)))
+        loads = [sum(lens[i] for i in p) for p in parts]
+        assert max(loads) / (sum(lens) / n) < 1.002
