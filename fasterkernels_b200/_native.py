@@ -80,8 +80,7 @@ def lib() -> ctypes.CDLL:
         L.fk_profile_begin.restype = _I
         L.fk_profile_begin.argtypes = [_I]
         L.fk_profile_end.restype = _I
-        L.fk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
-                                     ctypes.POINTER(_I)]
+        L.fk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I)]
         L.fk_decode_num_ctas.restype = _I
         L.fk_decode_num_ctas.argtypes = [_I, _I]
         _lib = L
@@ -159,13 +158,13 @@ def read_status(device=None, clear: bool = True) -> int:
 
 
 def profile_begin(max_launches: int) -> None:
-    """Record CUDA events around the split and combine passes of the next
+    """Record CUDA events around the decode kernel of the next
     ``max_launches`` decode calls (on their launching streams)."""
     check(lib().fk_profile_begin(int(max_launches)), "fk_profile_begin")
 
 
 def profile_end():
-    """Stop recording; returns (split_ms_total, combine_ms_total, calls)."""
-    a, b, n = ctypes.c_float(), ctypes.c_float(), ctypes.c_int()
-    check(lib().fk_profile_end(ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)), "fk_profile_end")
-    return a.value, b.value, n.value
+    """Stop recording; returns (kernel_ms_total, calls)."""
+    a, n = ctypes.c_float(), ctypes.c_int()
+    check(lib().fk_profile_end(ctypes.byref(a), ctypes.byref(n)), "fk_profile_end")
+    return a.value, n.value

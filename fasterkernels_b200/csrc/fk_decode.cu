@@ -1,5 +1,6 @@
-// fk_decode.cu -- B200 (sm_100a) GQA decode attention: split pass + combine
-// pass, behind the C-ABI declared in include/fk_decode.h.
+// fk_decode.cu -- B200 (sm_100a) GQA decode attention in one persistent
+// kernel (split-KV pass with an in-kernel sink-aware merge), behind the C-ABI
+// declared in include/fk_decode.h.
 //
 // Work decomposition ("stream-K" over KV granules).  Every (sequence b,
 // KV head h) pair is an item owning ceil(len_b / 16) granules of 16 tokens;
@@ -12,8 +13,10 @@
 // CUDA-graph safe).  The piece of item i inside CTA c is a segment with id
 // c + i (unique, < S + items).  A CTA that holds a whole item normalises and
 // writes the output itself; otherwise it stores the segment's (max, sum,
-// acc) partial and the combine kernel merges the partials of that item with
-// the sink term.
+// acc) partial in the workspace and bumps the item's arrival counter; the CTA
+// that brings the counter to the item's segment count merges the partials in
+// CTA order with the sink term (log-sum-exp combine) and re-arms the counter.
+// One launch per decode call; no CTA ever waits for another.
 //
 // Split pass, per CTA: one producer warp walks the plan and issues TMA tile
 // loads (64 tokens x 128 dims of K and of V per stage, 128-byte swizzled)
@@ -52,7 +55,8 @@ constexpr int TILE = 64;       // tokens per pipeline stage
 constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
 constexpr int THREADS = (CWARPS + 1) * 32;
 constexpr int PAGE = 16;       // tokens per granule (= page size)
-constexpr int MIN_PER = 4;     // minimum granules per CTA (one tile)
+constexpr int MIN_PER = 4;
+constexpr int FK_EMPTY = -1;  // internal: common_checks found an empty batch     // minimum granules per CTA (one tile)
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float NEG_INF = -__builtin_huge_valf();
 
@@ -74,28 +78,42 @@ struct KvCfg {
 };
 
 struct Meta {
-  int b, h, tok, valid, flags, seg, bad, pad;
+  int b, h, tok, valid, flags, seg, bad, c0, nseg, pad[3];
 };
 
-// Workspace layout (bytes): [0, 256) header, then pre[B+1] (int32 exclusive
-// prefix of granules per sequence), then ml[(S+I)*8] float2, then
-// acc[(S+I)*8*128] float.
+// Workspace layout (bytes), a function of the workspace SIZE W so that every
+// launch on one buffer agrees on where the arrival counters live:
+//   [0, 256)                 header (status word)
+//   [256, 256 + 4*cap)       cnt[cap]: per-item arrival counters, cap =
+//                            (W - 256) / SEG_BYTES; zero between launches
+//   ml  (aligned 256)        float2[(S+I)*8]  segment (max, sum)
+//   acc (aligned 256)        float[(S+I)*8*128] segment accumulators
+// A launch with I = B*KVH items fits when I <= cap and acc + its size <= W.
+// Partials of one launch can therefore never overwrite the counters another
+// launch (of any shape) uses on the same buffer.
 struct WsHeader {
   int status;
-  int pad0;
-  long long per;
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+constexpr size_t SEG_BYTES = 4 + GPAD * sizeof(float2) + GPAD * HEAD_DIM * sizeof(float);  // per segment (+1 counter)
+
 struct WsLayout {
-  size_t pre, ml, acc, total;
-  __host__ __device__ WsLayout(int B, int kvh, int S) {
-    size_t segs = static_cast<size_t>(S) + static_cast<size_t>(B) * kvh;
-    pre = 256;
-    ml = align_up(pre + 4 * (static_cast<size_t>(B) + 1), 256);
+  size_t cap, cnt, ml, acc, need;
+  WsLayout(size_t W, int B, int kvh, int S) {
+    const size_t segs = static_cast<size_t>(S) + static_cast<size_t>(B) * kvh;
+    cap = W > 256 ? (W - 256) / SEG_BYTES : 0;
+    cnt = 256;
+    ml = align_up(cnt + 4 * cap, 256);
     acc = align_up(ml + segs * GPAD * sizeof(float2), 256);
-    total = align_up(acc + segs * GPAD * HEAD_DIM * sizeof(float), 256);
+    need = acc + segs * GPAD * HEAD_DIM * sizeof(float);
+  }
+  bool fits(size_t W, int B, int kvh) const { return static_cast<size_t>(B) * kvh <= cap && need <= W; }
+  // Smallest buffer size whose own layout fits (B, kvh, S).
+  static size_t min_bytes(int B, int kvh, int S) {
+    const size_t segs = static_cast<size_t>(S) + static_cast<size_t>(B) * kvh;
+    return align_up(256 + segs * SEG_BYTES + 1024, 256);
   }
 };
 
@@ -111,6 +129,7 @@ struct Params {
   const int* bt;      // PAGED: block table
   long long bt_sb;
   long long max_tokens;  // DENSE: cache rows per sequence
+  long long ws_cnt, ws_ml, ws_acc;  // workspace region offsets (bytes)
   int max_blocks, num_pages;
   const float* s_aux;
   const float* scale_q;
@@ -196,10 +215,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   WsHeader* hdr = reinterpret_cast<WsHeader*>(p.ws);
-  const WsLayout wl(p.B, p.kv_heads, p.num_ctas);
-  int* pre = reinterpret_cast<int*>(p.ws + wl.pre);
-  float2* ws_ml = reinterpret_cast<float2*>(p.ws + wl.ml);
-  float* ws_acc = reinterpret_cast<float*>(p.ws + wl.acc);
+  int* cnt = reinterpret_cast<int*>(p.ws + p.ws_cnt);
+  float2* ws_ml = reinterpret_cast<float2*>(p.ws + p.ws_ml);
+  float* ws_acc = reinterpret_cast<float*>(p.ws + p.ws_acc);
+  __shared__ int s_last;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -217,23 +236,19 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
       prefetch_tmap(&p.tv);
     }
     const long long KVH = p.kv_heads;
-    // Plan: total granules and (CTA 0 only) the per-sequence prefix.
+    // Plan: total granules of the whole batch.
     long long tot = 0;
     for (int base = 0; base < p.B; base += 32) {
       const int b = base + lane;
       long long t0;
-      const long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
-      const long long inc = warp_incl_scan(n, lane);
-      if (blockIdx.x == 0 && b < p.B) pre[b] = static_cast<int>(tot + inc - n);
-      tot += __shfl_sync(0xffffffffu, inc, 31);
+      long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+      tot += n;
     }
     const long long U = tot * KVH;
     const long long S = p.num_ctas;
     const long long per = max((U + S - 1) / S, static_cast<long long>(MIN_PER));
-    if (blockIdx.x == 0 && lane == 0) {
-      pre[p.B] = static_cast<int>(tot);
-      hdr->per = per;
-    }
     const long long start = static_cast<long long>(blockIdx.x) * per;
     const long long end = min(start + per, U);
 
@@ -295,6 +310,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
         const int g1 = static_cast<int>(seg_hi - item_base);
         const bool whole = (item_base >= start) && (item_base + nb <= end);
         const int seg = blockIdx.x + b * p.kv_heads + h;
+        const int c0 = static_cast<int>(item_base / per);
+        const int nseg = static_cast<int>((item_base + nb - 1) / per) - c0 + 1;
         const int tbeg = g0 * PAGE;
         const int tend = min(g1 * PAGE, len);
         for (int tt = tbeg; tt < tend; tt += TILE) {
@@ -341,6 +358,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
             mt.flags = (tt == tbeg ? F_FIRST : 0) | (tt + TILE >= tend ? F_LAST : 0) | (whole ? F_WHOLE : 0);
             mt.seg = seg;
             mt.bad = bad;
+            mt.c0 = c0;
+            mt.nseg = nseg;
             mbar_arrive_expect_tx(fb, bytes);
           }
           __syncwarp();
@@ -404,6 +423,15 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
   const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
   const float sq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
+
+  // Sequences of length 0 own no granules: CTA b % S writes their zero rows.
+  for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
+    long long t0;
+    if (seq_len<LAYOUT>(p, b, &t0) == 0) {
+      for (int qh = 0; qh < p.q_heads; ++qh)
+        store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + threadIdx.x, 0.f);
+    }
+  }
 
   float m[2], l[2], acc[8][4];
   uint32_t qb[8][2];
@@ -601,6 +629,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
       }
       named_bar_sync(1, CWARPS * 32);
       const int d = threadIdx.x;  // 0..127
+      const bool whole = (mt.flags & F_WHOLE) != 0;
+      const long long item = static_cast<long long>(mt.b) * p.kv_heads + mt.h;
       for (int hd = 0; hd < p.G; ++hd) {
         float M = NEG_INF;
 #pragma unroll
@@ -609,19 +639,49 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
         if (M != NEG_INF) {
 #pragma unroll
           for (int w = 0; w < CWARPS; ++w) {
-            const float mw = cm[w * GPAD + hd];
-            const float e = exp2f(mw - M);
+            const float e = exp2f(cm[w * GPAD + hd] - M);
             A += e * cacc[(w * GPAD + hd) * HEAD_DIM + d];
             L += e * cl[w * GPAD + hd];
           }
         }
-        const int qh = mt.h * p.G + hd;
-        if (mt.flags & F_WHOLE) {
-          const float o = finalize(A, L, M, p.s_aux, qh, sv);
-          store_out(p, static_cast<long long>(mt.b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d, o);
+        if (whole) {
+          const int qh = mt.h * p.G + hd;
+          store_out(p, static_cast<long long>(mt.b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d,
+                    finalize(A, L, M, p.s_aux, qh, sv));
         } else {
           ws_acc[(static_cast<long long>(mt.seg) * GPAD + hd) * HEAD_DIM + d] = A;
           if (d == 0) ws_ml[static_cast<long long>(mt.seg) * GPAD + hd] = make_float2(M, L);
+        }
+      }
+      if (!whole) {
+        // Publish this segment; the CTA that completes the item merges all
+        // of its segments (in CTA order, so the result is deterministic) and
+        // re-arms the counter for the next launch.
+        __threadfence();
+        named_bar_sync(1, CWARPS * 32);
+        if (threadIdx.x == 0) s_last = (atomicAdd(&cnt[item], 1) == mt.nseg - 1) ? 1 : 0;
+        named_bar_sync(1, CWARPS * 32);
+        if (s_last) {
+          __threadfence();
+          for (int hd = 0; hd < p.G; ++hd) {
+            float M = NEG_INF;
+            for (int c = 0; c < mt.nseg; ++c)
+              M = fmaxf(M, __ldcg(&ws_ml[(item + mt.c0 + c) * GPAD + hd]).x);
+            float A = 0.f, L = 0.f;
+            if (M != NEG_INF) {
+              for (int c = 0; c < mt.nseg; ++c) {
+                const long long sg = item + mt.c0 + c;
+                const float2 ml = __ldcg(&ws_ml[sg * GPAD + hd]);
+                const float e = exp2f(ml.x - M);
+                A += e * __ldcg(&ws_acc[(sg * GPAD + hd) * HEAD_DIM + d]);
+                L += e * ml.y;
+              }
+            }
+            const int qh = mt.h * p.G + hd;
+            store_out(p, static_cast<long long>(mt.b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d,
+                      finalize(A, L, M, p.s_aux, qh, sv));
+          }
+          if (threadIdx.x == 0) cnt[item] = 0;
         }
       }
       named_bar_sync(1, CWARPS * 32);
@@ -634,66 +694,17 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
 }
 
 // ------------------------------------------------------------------------
-// Combine pass: one CTA (128 threads = head dims) per (sequence, KV head).
-// Merges the segment partials of items that span several CTAs and writes
-// the all-zero rows of empty sequences.
-// ------------------------------------------------------------------------
-template <int LAYOUT>
-__global__ void __launch_bounds__(128) decode_combine_kernel(const __grid_constant__ Params p) {
-  const int item = blockIdx.x;
-  const int b = item / p.kv_heads;
-  const int h = item % p.kv_heads;
-  const int d = threadIdx.x;
-  const WsHeader* hdr = reinterpret_cast<const WsHeader*>(p.ws);
-  const WsLayout wl(p.B, p.kv_heads, p.num_ctas);
-  const int* pre = reinterpret_cast<const int*>(p.ws + wl.pre);
-  const float2* ws_ml = reinterpret_cast<const float2*>(p.ws + wl.ml);
-  const float* ws_acc = reinterpret_cast<const float*>(p.ws + wl.acc);
-  long long tok0;
-  const int len = seq_len<LAYOUT>(p, b, &tok0);
-  const long long nb = (len + PAGE - 1) / PAGE;
-  if (nb == 0) {
-    for (int hd = 0; hd < p.G; ++hd) {
-      const int qh = h * p.G + hd;
-      store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d, 0.f);
-    }
-    return;
-  }
-  const long long per = hdr->per;
-  const long long P = static_cast<long long>(p.kv_heads) * pre[b] + static_cast<long long>(h) * nb;
-  const long long c0 = P / per, c1 = (P + nb - 1) / per;
-  if (c0 == c1) return;  // written by the split pass
-  const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
-  for (int hd = 0; hd < p.G; ++hd) {
-    float M = NEG_INF;
-    for (long long c = c0; c <= c1; ++c) M = fmaxf(M, ws_ml[(c + item) * GPAD + hd].x);
-    float A = 0.f, L = 0.f;
-    if (M != NEG_INF) {
-      for (long long c = c0; c <= c1; ++c) {
-        const float2 ml = ws_ml[(c + item) * GPAD + hd];
-        const float e = exp2f(ml.x - M);
-        A += e * ws_acc[((c + item) * GPAD + hd) * HEAD_DIM + d];
-        L += e * ml.y;
-      }
-    }
-    const int qh = h * p.G + hd;
-    store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d,
-              finalize(A, L, M, p.s_aux, qh, sv));
-  }
-}
-
-// ------------------------------------------------------------------------
 // Host side.
 // ------------------------------------------------------------------------
 thread_local std::string g_err;
 
-// Optional per-launch timing: when enabled, three events are recorded on the
-// launching stream around each split pass and combine pass.
+// Optional per-launch timing: when enabled, events are recorded on the
+// launching stream just before and just after each decode kernel.
 struct Profiler {
   std::mutex mu;
   bool on = false;
   int cap = 0, n = 0;
-  cudaEvent_t* ev = nullptr;  // 3 per launch
+  cudaEvent_t* ev = nullptr;  // 2 per launch
 };
 Profiler g_prof;
 
@@ -701,8 +712,8 @@ void prof_mark(int which, cudaStream_t stream) {
   if (!g_prof.on) return;
   std::lock_guard<std::mutex> lk(g_prof.mu);
   if (!g_prof.on || g_prof.n >= g_prof.cap) return;
-  cudaEventRecord(g_prof.ev[3 * g_prof.n + which], stream);
-  if (which == 2) ++g_prof.n;
+  cudaEventRecord(g_prof.ev[2 * g_prof.n + which], stream);
+  if (which == 1) ++g_prof.n;
 }
 
 int fail(int code, const char* fmt, ...) {
@@ -819,6 +830,7 @@ bool is16(int dt) { return dt == FK_DTYPE_F16 || dt == FK_DTYPE_BF16; }
 
 int common_checks(const void* q, const void* k, const void* v, const void* out, int batch, int q_heads, int kv_heads,
                   int head_dim, int q_dtype, int kv_dtype, int out_dtype, void* ws, int* device) {
+  if (batch == 0) return FK_EMPTY;  // nothing to do; pointers of empty tensors may be null
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
     return fail(FK_ERR_INVALID_ARG, "q, k, v and out must be non-null");
   if (ws == nullptr) return fail(FK_ERR_WORKSPACE, "workspace must be non-null");
@@ -852,9 +864,13 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   const int S = num_work_ctas(device, kv);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   p.num_ctas = S;
-  const WsLayout wl(p.B, p.kv_heads, S);
-  if (ws_bytes < wl.total)
-    return fail(FK_ERR_WORKSPACE, "workspace too small: %zu bytes < %zu required", ws_bytes, wl.total);
+  const WsLayout wl(ws_bytes, p.B, p.kv_heads, S);
+  if (!wl.fits(ws_bytes, p.B, p.kv_heads))
+    return fail(FK_ERR_WORKSPACE, "workspace too small: %zu bytes < %zu required", ws_bytes,
+                WsLayout::min_bytes(p.B, p.kv_heads, S));
+  p.ws_cnt = static_cast<long long>(wl.cnt);
+  p.ws_ml = static_cast<long long>(wl.ml);
+  p.ws_acc = static_cast<long long>(wl.acc);
   if (p.B == 0) return FK_OK;
   int prev = 0;
   cudaGetDevice(&prev);
@@ -880,8 +896,6 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   }
   if (rc == FK_OK) {
     prof_mark(1, stream);
-    decode_combine_kernel<LAYOUT><<<p.B * p.kv_heads, 128, 0, stream>>>(p);
-    prof_mark(2, stream);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = fail(FK_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
   }
@@ -932,7 +946,7 @@ extern "C" size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads,
     fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
     return 0;
   }
-  return WsLayout(batch, kv_heads, S).total;
+  return WsLayout::min_bytes(batch, kv_heads, S);
 }
 
 extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, const void* v_varlen,
@@ -944,6 +958,7 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
   int device = 0;
   int rc = common_checks(q, k_varlen, v_varlen, out, batch, q_heads, kv_heads, head_dim, dtype, dtype, dtype,
                          workspace, &device);
+  if (rc == FK_EMPTY) return FK_OK;
   if (rc != FK_OK) return rc;
   if (!is16(dtype)) return fail(FK_ERR_UNSUPPORTED, "varlen decode takes f16 or bf16 tensors");
   if (cu_seqlens_k == nullptr) return fail(FK_ERR_INVALID_ARG, "cu_seqlens_k must be non-null");
@@ -977,6 +992,7 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
   int device = 0;
   int rc = common_checks(q, k_cache, v_cache, out, batch, q_heads, kv_heads, head_dim, q_dtype, kv_dtype, out_dtype,
                          workspace, &device);
+  if (rc == FK_EMPTY) return FK_OK;
   if (rc != FK_OK) return rc;
   if (cache_lens == nullptr) return fail(FK_ERR_INVALID_ARG, "cache_lens must be non-null");
   if (max_seqlen <= 0 || max_seqlen > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad max_seqlen");
@@ -1015,6 +1031,7 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   int device = 0;
   int rc = common_checks(q, k_pool, v_pool, out, batch, q_heads, kv_heads, head_dim, q_dtype, kv_dtype, out_dtype,
                          workspace, &device);
+  if (rc == FK_EMPTY) return FK_OK;
   if (rc != FK_OK) return rc;
   if (page_size != PAGE) return fail(FK_ERR_UNSUPPORTED, "page_size must be 16 (got %d)", page_size);
   if (block_table == nullptr || seq_lens == nullptr)
@@ -1049,14 +1066,17 @@ extern "C" int fk_profile_begin(int max_launches) {
   std::lock_guard<std::mutex> lk(g_prof.mu);
   if (max_launches <= 0) return fail(FK_ERR_INVALID_ARG, "max_launches must be positive");
   if (g_prof.ev != nullptr) {
-    for (int i = 0; i < 3 * g_prof.cap; ++i) cudaEventDestroy(g_prof.ev[i]);
+    for (int i = 0; i < 2 * g_prof.cap; ++i) cudaEventDestroy(g_prof.ev[i]);
     delete[] g_prof.ev;
   }
-  g_prof.ev = new cudaEvent_t[3 * max_launches];
-  for (int i = 0; i < 3 * max_launches; ++i) {
+  g_prof.ev = new cudaEvent_t[2 * max_launches];
+  for (int i = 0; i < 2 * max_launches; ++i) {
     const cudaError_t e = cudaEventCreate(&g_prof.ev[i]);
     if (e != cudaSuccess) {
-      g_prof.cap = i / 3;
+      for (int j = 0; j < i; ++j) cudaEventDestroy(g_prof.ev[j]);
+      delete[] g_prof.ev;
+      g_prof.ev = nullptr;
+      g_prof.cap = 0;
       g_prof.on = false;
       return fail(FK_ERR_CUDA, "cudaEventCreate: %s", cudaGetErrorString(e));
     }
@@ -1067,20 +1087,17 @@ extern "C" int fk_profile_begin(int max_launches) {
   return FK_OK;
 }
 
-extern "C" int fk_profile_end(float* split_ms, float* combine_ms, int* launches) {
+extern "C" int fk_profile_end(float* kernel_ms, int* launches) {
   std::lock_guard<std::mutex> lk(g_prof.mu);
   g_prof.on = false;
-  float s = 0.f, c = 0.f;
+  float total = 0.f;
   for (int i = 0; i < g_prof.n; ++i) {
-    float a = 0.f, b = 0.f;
-    if (cudaEventSynchronize(g_prof.ev[3 * i + 2]) != cudaSuccess) return fail(FK_ERR_CUDA, "event sync failed");
-    cudaEventElapsedTime(&a, g_prof.ev[3 * i], g_prof.ev[3 * i + 1]);
-    cudaEventElapsedTime(&b, g_prof.ev[3 * i + 1], g_prof.ev[3 * i + 2]);
-    s += a;
-    c += b;
+    float a = 0.f;
+    if (cudaEventSynchronize(g_prof.ev[2 * i + 1]) != cudaSuccess) return fail(FK_ERR_CUDA, "event sync failed");
+    cudaEventElapsedTime(&a, g_prof.ev[2 * i], g_prof.ev[2 * i + 1]);
+    total += a;
   }
-  if (split_ms) *split_ms = s;
-  if (combine_ms) *combine_ms = c;
+  if (kernel_ms) *kernel_ms = total;
   if (launches) *launches = g_prof.n;
   return FK_OK;
 }

@@ -18,8 +18,11 @@
  *  - The innermost (head_dim) stride of every tensor is 1; K/V base pointers
  *    and their strides in bytes must be multiples of 16 (TMA rule).
  *  - Nothing is synchronised with the host and nothing is allocated: the
- *    call enqueues two kernels on `stream` (split pass + combine pass) and
- *    returns.  It is safe to capture in a CUDA graph once `workspace` exists.
+ *    call enqueues one kernel on `stream` and returns.  It is safe to capture
+ *    in a CUDA graph once `workspace` exists.
+ *  - The workspace also carries per-(sequence, KV head) arrival counters
+ *    that each launch leaves at zero; calls sharing a workspace must be
+ *    stream-ordered, and a new workspace must start zeroed.
  *  - `workspace` is caller-owned device memory of at least
  *    fk_decode_workspace_bytes(...) bytes.  Its first int32 is a sticky
  *    status word (FK_STATUS_*) that kernels OR into; the caller clears it.
@@ -150,14 +153,13 @@ int fk_paged_flash_decode(const void* q, const void* k_pool, const void* v_pool,
 /*
  * Measurement hooks (no reference counterpart: the reference times with
  * torch.profiler / triton.testing.do_bench, benchmarks/benchmark.py:87-91).
- * fk_profile_begin(n) records CUDA events on the launching stream before the
- * split pass, between the passes and after the combine pass of the next n
- * decode calls made from any thread; fk_profile_end() stops recording, waits
- * for the events and returns the summed split / combine milliseconds and the
- * number of calls recorded.
+ * fk_profile_begin(n) records CUDA events on the launching stream just before
+ * and just after the decode kernel of the next n decode calls made from any
+ * thread; fk_profile_end() stops recording, waits for the events and returns
+ * the summed kernel milliseconds and the number of calls recorded.
  */
 int fk_profile_begin(int max_launches);
-int fk_profile_end(float* split_ms, float* combine_ms, int* launches);
+int fk_profile_end(float* kernel_ms, int* launches);
 
 /* Size of the persistent split-pass grid (resident CTAs) on `device`. */
 int fk_decode_num_ctas(int device, int kv_dtype);

@@ -122,6 +122,29 @@ def test_long_single_sequence_spans_many_ctas(dev):
     close(out, _oracle(q, k, v, cu, s), **F16_TOL)
 
 
+def test_workspace_counters_rearmed(dev):
+    # every launch leaves the per-item arrival counters at zero
+    q, k, v, cu, s = _rand_case(dev, [9000, 12000, 5], 32, 8, torch.float16, True, seed=12)
+    for _ in range(3):
+        fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    torch.cuda.synchronize()
+    ws = N._ws[dev.index]
+    assert int(ws[256:256 + 4 * 3 * 8].view(torch.int32).abs().sum()) == 0
+
+
+def test_workspace_shared_across_shapes(dev):
+    # launches of different (B, KV_H) on one workspace must not disturb each
+    # other's arrival counters: small batch first, then a larger split batch
+    for lens, qh, kvh in (([900, 40], 8, 2), ([6000] * 40, 32, 8), ([30, 7000, 3], 16, 4), ([6000] * 40, 32, 8)):
+        q, k, v, cu, s = _rand_case(dev, lens, qh, kvh, torch.float16, True, seed=len(lens))
+        out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+        b = len(lens) - 1
+        lo, hi = int(cu[b]), int(cu[b + 1])
+        ref = O.decode_varlen(q[b:b + 1].float().cpu().numpy(), k[lo:hi].float().cpu().numpy(),
+                              v[lo:hi].float().cpu().numpy(), np.array([0, hi - lo]), s.cpu().numpy())
+        close(out[b:b + 1], ref, **F16_TOL)
+
+
 def test_many_short_sequences(dev):
     lens = [int(x) for x in torch.randint(0, 40, (700,), generator=torch.Generator().manual_seed(5))]
     q, k, v, cu, s = _rand_case(dev, lens, 16, 4, torch.float16, True, seed=5)
