@@ -1103,3 +1103,85 @@ extern "C" int fk_profile_end(float* kernel_ms, int* launches) {
 }
 
 extern "C" int fk_decode_num_ctas(int device, int kv_dtype) { return num_work_ctas(device, kv_dtype); }
+
+// ==========================================================================
+// Allocation-free variant of the varlen decode.
+//
+// For callers that must not allocate device memory at all -- for example a
+// plugin that runs inside a host framework owning every allocation, or code
+// running where cudaMalloc is forbidden after start-up -- the scratch
+// (status word, arrival counters, segment partials) lives in the file-scope
+// array below instead of a caller-provided workspace.  Every GPU that loads
+// this library holds the array until the process exits.
+// ==========================================================================
+namespace fk {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(8) << 20;  // 8 MiB: up to ~2000 segments
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch, resolved once per device.  In host code
+// the array's name is only a host-side stand-in, never a device pointer.
+int noalloc_scratch(int device, void** out) {
+  static void* addr[64] = {};
+  static std::mutex mu;
+  if (device < 0 || device >= 64) return fail(FK_ERR_INVALID_ARG, "device index %d out of range", device);
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[device] == nullptr) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != device) cudaSetDevice(device);
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(FK_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+    addr[device] = p;
+  }
+  *out = addr[device];
+  return FK_OK;
+}
+
+}  // namespace fk
+
+extern "C" size_t fk_noalloc_scratch_bytes(void) { return NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_varlen, const void* v_varlen,
+                                                  const int32_t* cu_seqlens_k, const float* s_aux, void* out,
+                                                  int batch, int q_heads, int kv_heads, int head_dim,
+                                                  int64_t total_tokens, int dtype, int64_t sq_b, int64_t sq_h,
+                                                  int64_t sk_t, int64_t sk_h, int64_t sv_t, int64_t sv_h,
+                                                  int64_t so_b, int64_t so_h, void* stream) {
+  if (batch == 0) return FK_OK;
+  if (k_varlen == nullptr) return fail(FK_ERR_INVALID_ARG, "q, k, v and out must be non-null");
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, k_varlen) != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return fail(FK_ERR_INVALID_ARG, "k must be device memory");
+  }
+  const int device = attr.device;
+  if (batch < 0 || kv_heads <= 0) return fail(FK_ERR_INVALID_ARG, "bad sizes: batch=%d kv_heads=%d", batch, kv_heads);
+  const int S = num_work_ctas(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16);
+  if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
+  const size_t need = WsLayout::min_bytes(batch, kv_heads, S);
+  if (need > NOALLOC_SCRATCH_BYTES)
+    return fail(FK_ERR_WORKSPACE,
+                "batch*kv_heads = %lld needs %zu bytes of scratch; the allocation-free entry point has a fixed "
+                "%zu-byte scratch (batch*kv_heads + %d <= %zu)",
+                static_cast<long long>(batch) * kv_heads, need, NOALLOC_SCRATCH_BYTES, S,
+                (NOALLOC_SCRATCH_BYTES - 256 - 1024) / SEG_BYTES);
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(device, &scratch);
+  if (rc != FK_OK) return rc;
+  // The status word and the arrival counters must start at zero: clear them on
+  // the caller's stream (a memset, not an allocation).
+  const WsLayout wl(NOALLOC_SCRATCH_BYTES, batch, kv_heads, S);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, wl.ml, static_cast<cudaStream_t>(stream));
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(FK_ERR_CUDA, "clearing the scratch failed: %s", cudaGetErrorString(e));
+  return fk_flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux, out, batch, q_heads, kv_heads,
+                                    head_dim, total_tokens, dtype, sq_b, sq_h, sk_t, sk_h, sv_t, sv_h, so_b, so_h,
+                                    scratch, NOALLOC_SCRATCH_BYTES, stream);
+}

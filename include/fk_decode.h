@@ -161,6 +161,33 @@ int fk_paged_flash_decode(const void* q, const void* k_pool, const void* v_pool,
 int fk_profile_begin(int max_launches);
 int fk_profile_end(float* kernel_ms, int* launches);
 
+/*
+ * Allocation-free varlen decode (no counterpart in the reference).
+ * Same arguments and result as fk_flash_decode_gqa_varlen, without the
+ * workspace: for callers that cannot allocate device memory -- a plugin whose
+ * host framework owns every allocation, or a process where cudaMalloc is not
+ * allowed once serving starts -- the scratch comes from a fixed array inside
+ * the library (fk_noalloc_scratch_bytes() bytes, 8 MiB, held on every GPU that
+ * loads the library until exit).  It fits batch * kv_heads + (resident CTAs)
+ * <= about 2000 segments; larger calls return FK_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  Each call clears the scratch's
+ * status word and counters on `stream`.  All calls share the one array, so
+ * calls that overlap on the GPU (different streams, or different threads)
+ * race: serialise them.  Nothing is allocated: no cudaMalloc/cudaFree.
+ */
+int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_varlen, const void* v_varlen,
+                                       const int32_t* cu_seqlens_k, const float* s_aux, void* out,
+                                       int batch, int q_heads, int kv_heads, int head_dim,
+                                       int64_t total_tokens, int dtype,
+                                       int64_t sq_b, int64_t sq_h,
+                                       int64_t sk_t, int64_t sk_h,
+                                       int64_t sv_t, int64_t sv_h,
+                                       int64_t so_b, int64_t so_h, void* stream);
+
+/* Bytes of the fixed scratch used by fk_flash_decode_gqa_varlen_noalloc. */
+size_t fk_noalloc_scratch_bytes(void);
+
 /* Size of the persistent split-pass grid (resident CTAs) on `device`. */
 int fk_decode_num_ctas(int device, int kv_dtype);
 
