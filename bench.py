@@ -125,6 +125,63 @@ def setup_workload(name, rank, world, device):
                "parallelism": f"dp{world} (each rank its own batch, no collective)"}
         return dict(run=run, q=q, lens_dev=cu, out=out, kv_bytes=kvb, cfg=cfg, scaling="weak",
                     sample=(q, k, v, cu, s, lens), dtype="fp16 in / fp32 accumulate")
+    if name == "config3v":  # config-3 lengths in the contiguous varlen layout (comparison / profiling)
+        spec = W.CONFIGS[3]
+        lens = W.config_lengths(3, seed=rank)
+        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=False)
+        q, k, v, cu = d["q"], d["k"], d["v"], d["cu_seqlens"]
+        out = torch.empty_like(q)
+
+        def run(qq=q, cc=cu, oo=out):
+            return fk.flash_decode_gqa_varlen(qq, k, v, cc, out=oo)
+        cfg = {"workload": spec.name + "_as_varlen", "batch_per_gpu": spec.batch, "global_batch": spec.batch * world,
+               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
+               "seq_lens": "U[512,8192], seed = rank", "kv_layout": "contiguous varlen fp16", "sinks": False,
+               "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
+        return dict(run=run, q=q, lens_dev=cu, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 2), cfg=cfg,
+                    scaling="weak", sample=None, dtype="fp16 in / fp32 accumulate")
+    if name == "config3":
+        spec = W.CONFIGS[3]
+        lens = W.config_lengths(3, seed=rank)
+        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=False)
+        kp, vp, bt = W.varlen_to_paged(d["k"], d["v"], lens, spec.pool_factor, seed=rank)
+        del d["k"], d["v"]
+        q = d["q"]
+        sl = torch.tensor(lens, dtype=torch.int32, device=device)
+        out = torch.empty_like(q)
+
+        def run(qq=q, ll=sl, oo=out):
+            return fk.paged_flash_decode(qq, kp, vp, bt, ll, 16, out=oo)
+        cfg = {"workload": spec.name, "batch_per_gpu": spec.batch, "global_batch": spec.batch * world,
+               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
+               "seq_lens": "U[512,8192], seed = rank", "pool_pages": int(kp.shape[0]),
+               "kv_layout": "paged 16-token pages (random permutation of a x1.25 pool), fp16", "sinks": False,
+               "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
+        return dict(run=run, q=q, lens_dev=sl, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 2), cfg=cfg,
+                    scaling="weak", sample=None, dtype="fp16 in / fp32 accumulate")
+    if name == "config4":
+        spec = W.CONFIGS[4]
+        lens = W.config_lengths(4, seed=rank)
+        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
+        k8, sk = W.quantize_e4m3(d["k"])
+        del d["k"]
+        v8, sv = W.quantize_e4m3(d["v"])
+        del d["v"]
+        kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.0, seed=rank)
+        del k8, v8
+        kp, vp = kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn)
+        q, s = d["q"], d["s_aux"]
+        sl = torch.tensor(lens, dtype=torch.int32, device=device)
+        out = torch.empty_like(q)
+
+        def run(qq=q, ll=sl, oo=out):
+            return fk.paged_flash_decode(qq, kp, vp, bt, ll, 16, s_aux=s, scale_k=sk, scale_v=sv, out=oo)
+        cfg = {"workload": spec.name, "batch_per_gpu": spec.batch, "global_batch": spec.batch * world,
+               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128, "seq_lens": "32768 all",
+               "kv_layout": "paged 16-token pages, e4m3 KV (per-tensor scale amax/448), fp16 Q", "sinks": True,
+               "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
+        return dict(run=run, q=q, lens_dev=sl, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 1), cfg=cfg,
+                    scaling="weak", sample=None, dtype="e4m3 KV / fp16 Q / fp32 accumulate")
     if name == "config5":
         spec = W.CONFIGS[5]
         all_lens = W.config_lengths(5, seed=0)
@@ -314,10 +371,10 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     from oracle import gqa_decode_oracle as O
-    if args.workload == "config5":
-        spec = W.CONFIGS[5]
-        lens = W.config_lengths(5, seed=0)
-        kvh, qh, es = spec.kv_heads, spec.q_heads, 1
+    if args.workload in ("config3", "config3v", "config4", "config5"):
+        spec = W.CONFIGS[int(args.workload[6])]
+        lens = W.config_lengths(spec, seed=0)
+        kvh, qh, es = spec.kv_heads, spec.q_heads, (1 if spec.kv_dtype == torch.float8_e4m3fn else 2)
     else:
         spec = W.CONFIGS[2]
         lens = W.config_lengths(2, seed=0)
@@ -354,7 +411,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["config2", "config2s", "config5"], default="config2")
+    ap.add_argument("--workload", choices=["config2", "config2s", "config3", "config3v", "config4", "config5"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

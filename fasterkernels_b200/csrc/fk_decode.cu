@@ -53,7 +53,9 @@ constexpr int HEAD_DIM = 128;
 constexpr int GPAD = 8;        // MMA N: query heads of one KV group, padded
 constexpr int TILE = 64;       // tokens per pipeline stage
 constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
-constexpr int THREADS = (CWARPS + 1) * 32;
+constexpr int EWARPS = 2;      // epilogue warps: segment merge / output / partials
+constexpr int THREADS = (CWARPS + 1 + EWARPS) * 32;
+constexpr int ETHREADS = EWARPS * 32;
 constexpr int PAGE = 16;       // tokens per granule (= page size)
 constexpr int MIN_PER = 4;
 constexpr int FK_EMPTY = -1;  // internal: common_checks found an empty batch     // minimum granules per CTA (one tile)
@@ -75,6 +77,31 @@ struct KvCfg {
   static constexpr int BOX_D = FP8 ? 128 : 64;               // dims per TMA box (128 bytes)
   static constexpr int NHALF = HEAD_DIM / BOX_D;             // boxes per 128-dim row
   static constexpr int HALF_BYTES = TILE * 128;              // one [64 rows][128 B] box region
+  static constexpr int MINB = FP8 ? 2 : 1;                   // resident CTAs per SM
+};
+
+// One epilogue slot: the four consumer warps' online-softmax states of a
+// finished segment, handed to the epilogue warps.
+struct EpiSlot {
+  float cm[CWARPS][GPAD];
+  float cl[CWARPS][GPAD];
+  float cacc[CWARPS][GPAD][HEAD_DIM];
+};
+
+// Shared-memory tile layouts of a 64-token K (or V) stage, 128-byte swizzled
+// (16-byte chunk index XOR row & 7).  16-bit KV stores two 64-dim halves:
+//   VARLEN / DENSE: [half][64 rows][64 dims]      (one 8 KB TMA box per half)
+//   PAGED:          [page][half][16 rows][64 dims] (one 4 KB TMA box per page)
+// FP8 KV stores [64 rows][128 dims] for every layout.  Row r, 16-byte chunk c
+// of the 256-byte (16-bit) row is at row_off(r) + (c >> 3) * half_stride +
+// (((c & 7) ^ (r & 7)) << 4).
+template <int KV, int LAYOUT>
+struct TileLayout {
+  static constexpr bool GROUPED = (LAYOUT == 2 /* PAGED */) && KV != FK_DTYPE_E4M3;
+  static constexpr uint32_t HALF_STRIDE = GROUPED ? 2048u : uint32_t(TILE * 128);
+  __device__ static __forceinline__ uint32_t row_off(int r) {
+    return GROUPED ? uint32_t((r >> 4) * 4096 + (r & 15) * 128) : uint32_t(r * 128);
+  }
 };
 
 struct Meta {
@@ -168,12 +195,33 @@ __device__ __forceinline__ long long warp_incl_scan(long long v, int lane) {
   return v;
 }
 
-__device__ __forceinline__ float load_q_elem(const Params& p, long long idx, float sq) {
-  if (p.q_dtype == FK_DTYPE_F16) return __half2float(static_cast<const __half*>(p.q)[idx]);
-  if (p.q_dtype == FK_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p.q)[idx]);
-  const __nv_fp8_storage_t v = static_cast<const __nv_fp8_storage_t*>(p.q)[idx];
-  const __half_raw hr = __nv_cvt_fp8_to_halfraw(v, __NV_E4M3);
-  return __half2float(__half(hr)) * sq;
+// Two adjacent Q elements (even element index e) as raw bits: 32 bits for
+// 16-bit Q, 16 bits for e4m3 Q.  Strides and the base are validated on the
+// host to keep these loads aligned.
+__device__ __forceinline__ uint32_t load_q_pair_raw(const Params& p, long long e) {
+  if (p.q_dtype == FK_DTYPE_E4M3) return __ldg(reinterpret_cast<const unsigned short*>(static_cast<const unsigned char*>(p.q) + e));
+  return __ldg(reinterpret_cast<const uint32_t*>(static_cast<const unsigned short*>(p.q) + e));
+}
+
+// Raw Q pair -> packed pair of the MMA element type.
+template <bool MBF16>
+__device__ __forceinline__ uint32_t q_pair_to_mma(const Params& p, uint32_t raw, float sq) {
+  if (p.q_dtype == (MBF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16)) return raw;
+  float x0, x1;
+  if (p.q_dtype == FK_DTYPE_E4M3) {
+    x0 = __half2float(__half(__nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(raw & 0xff), __NV_E4M3))) * sq;
+    x1 = __half2float(__half(__nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>((raw >> 8) & 0xff), __NV_E4M3))) * sq;
+  } else if (p.q_dtype == FK_DTYPE_BF16) {
+    x0 = __uint_as_float(raw << 16);
+    x1 = __uint_as_float(raw & 0xffff0000u);
+  } else {
+    __half_raw a, b2;
+    a.x = static_cast<unsigned short>(raw & 0xffff);
+    b2.x = static_cast<unsigned short>(raw >> 16);
+    x0 = __half2float(__half(a));
+    x1 = __half2float(__half(b2));
+  }
+  return pack2<MBF16>(x0, x1);
 }
 
 __device__ __forceinline__ void store_out(const Params& p, long long idx, float v) {
@@ -196,21 +244,35 @@ __device__ __forceinline__ float finalize(float A, float L, float M, const float
   return L > 0.f ? (A / L) * sv : 0.f;
 }
 
+#ifdef FK_TRACE
+// Per-CTA timeline for performance investigation builds (-DFK_TRACE):
+// [start, first tile, end (ns), segments, tiles, producer switch ns, producer acquire-wait ns,
+//  consumer wait ns at first tiles of segments, consumer wait ns at other tiles, 0]
+__device__ unsigned long long g_trace[4096][10];
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#endif
+
 // ------------------------------------------------------------------------
 // Split pass.
 // ------------------------------------------------------------------------
 template <int KV, int LAYOUT>
-__global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
   using C = KvCfg<KV>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* stages = smem;
-  float* cacc = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);        // [CWARPS][GPAD][128]
-  float* cm = cacc + CWARPS * GPAD * HEAD_DIM;                                      // [CWARPS][GPAD]
-  float* cl = cm + CWARPS * GPAD;                                                   // [CWARPS][GPAD]
-  Meta* meta = reinterpret_cast<Meta*>(cl + CWARPS * GPAD);                          // [STAGES]
-  uint64_t* full = reinterpret_cast<uint64_t*>(meta + C::STAGES);                   // [STAGES]
+  EpiSlot* eslot = reinterpret_cast<EpiSlot*>(smem + C::STAGES * C::STAGE_BYTES);  // [2]
+  Meta* emeta = reinterpret_cast<Meta*>(eslot + 2);                                  // [2]
+  Meta* meta = emeta + 2;                                                            // [STAGES]
+  uint32_t* qstage = reinterpret_cast<uint32_t*>(meta + C::STAGES);                 // [STAGES][GPAD*64] (f16x2/bf16x2)
+  uint64_t* full = reinterpret_cast<uint64_t*>(qstage + C::STAGES * GPAD * 64);     // [STAGES]
   uint64_t* empty = full + C::STAGES;                                               // [STAGES]
+  uint64_t* efull = empty + C::STAGES;                                              // [2]
+  uint64_t* eempty = efull + 2;                                                     // [2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -220,10 +282,22 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
   float* ws_acc = reinterpret_cast<float*>(p.ws + p.ws_acc);
   __shared__ int s_last;
 
+#ifdef FK_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 4096) {
+    for (int i = 1; i < 10; ++i) g_trace[blockIdx.x][i] = 0;
+    g_trace[blockIdx.x][0] = gtimer();
+  }
+  unsigned long long tr_nseg = 0, tr_ntile = 0;
+  bool tr_first = true;
+#endif
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), CWARPS);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&efull[s]), CWARPS * 32);
+      mbar_init(smem_u32(&eempty[s]), ETHREADS);
     }
     fence_mbar_init();
   }
@@ -236,6 +310,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
       prefetch_tmap(&p.tv);
     }
     const long long KVH = p.kv_heads;
+    const float psq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
     // Plan: total granules of the whole batch.
     long long tot = 0;
     for (int base = 0; base < p.B; base += 32) {
@@ -258,7 +333,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
     // Claim the next ring slot (waits for the consumers to release it).
     auto acquire = [&]() -> bool {
       int ok = 1;
+#ifdef FK_TRACE
+      const unsigned long long tq0 = gtimer();
+#endif
       if (lane == 0) ok = mbar_wait(smem_u32(&empty[stage]), phase ^ 1u) ? 1 : 0;
+#ifdef FK_TRACE
+      if (lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][6] += gtimer() - tq0;
+#endif
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok && lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
       return ok != 0;
@@ -296,6 +377,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
       long long item_base = KVH * preb + static_cast<long long>(h) * nb;
       long long pos = start;
 
+      // Q words of the next item, prefetched into registers (lane owns words
+      // lane + 32k of the [8 heads][64 pairs] block).
+      constexpr int QW = GPAD * 64 / 32;
+      uint32_t qpre[QW];
+      int qpre_b = -1, qpre_h = -1;
+      auto q_prefetch = [&](int bb, int hh) {
+        const long long qb0 = static_cast<long long>(bb) * p.q_sb;
+#pragma unroll
+        for (int k = 0; k < QW; ++k) {
+          const int idx = lane + 32 * k;
+          const int j = idx >> 6, d = (idx & 63) * 2;
+          qpre[k] = (j < p.G) ? load_q_pair_raw(p, qb0 + static_cast<long long>(hh * p.G + j) * p.q_sh + d) : 0u;
+        }
+        qpre_b = bb;
+        qpre_h = hh;
+      };
+      // length of the next sequence, prefetched
+      long long ntok0 = 0;
+      int nlen = (b + 1 < p.B) ? seq_len<LAYOUT>(p, b + 1, &ntok0) : 0;
+
       // PAGED: window of 32 block-table entries (one per lane) + the next one.
       int win_b = -1;
       int win_p0 = 0;
@@ -314,6 +415,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
         const int nseg = static_cast<int>((item_base + nb - 1) / per) - c0 + 1;
         const int tbeg = g0 * PAGE;
         const int tend = min(g1 * PAGE, len);
+#ifdef FK_TRACE
+        unsigned long long tr_sw0 = gtimer();
+#endif
         for (int tt = tbeg; tt < tend; tt += TILE) {
           const int valid = min(TILE, tend - tt);
           if (!acquire()) {
@@ -349,6 +453,19 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
             if (lane == 0 && bad) atomicOr(&hdr->status, FK_STATUS_BAD_PAGE);
             if (!okp) phys = -1;
           }
+          if (tt == tbeg) {
+            // Q rows of item (b, h) -> qstage[stage] as packed MMA-type pairs,
+            // from the registers prefetched one item ahead
+            if (qpre_b != b || qpre_h != h) q_prefetch(b, h);
+            uint32_t* qs = qstage + stage * (GPAD * 64);
+#pragma unroll
+            for (int k = 0; k < QW; ++k) qs[lane + 32 * k] = q_pair_to_mma<C::BF16>(p, qpre[k], psq);
+            // start fetching the next item's Q
+            if (h + 1 < p.kv_heads) q_prefetch(b, h + 1);
+            else if (b + 1 < p.B) q_prefetch(b + 1, 0);
+            __threadfence_block();
+            __syncwarp();
+          }
           if (lane == 0) {
             Meta& mt = meta[stage];
             mt.b = b;
@@ -365,11 +482,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
           __syncwarp();
           if constexpr (LAYOUT == PAGED) {
             if (phys >= 0) {
-#pragma unroll
-              for (int hf = 0; hf < C::NHALF; ++hf) {
-                const uint32_t off = hf * C::HALF_BYTES + lane * (PAGE * 128);
-                tma_load_4d(sK + off, &p.tk, fb, hf * C::BOX_D, 0, h, phys);
-                tma_load_4d(sV + off, &p.tv, fb, hf * C::BOX_D, 0, h, phys);
+              // one box per page-head: 16 tokens x 128 dims
+              const uint32_t off = lane * (PAGE * 128 * C::ES);
+              if constexpr (C::FP8) {
+                tma_load_4d(sK + off, &p.tk, fb, 0, 0, h, phys);
+                tma_load_4d(sV + off, &p.tv, fb, 0, 0, h, phys);
+              } else {
+                tma_load_5d(sK + off, &p.tk, fb, 0, 0, 0, h, phys);
+                tma_load_5d(sV + off, &p.tv, fb, 0, 0, 0, h, phys);
               }
             }
           } else if (lane == 0) {
@@ -387,6 +507,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
               }
             }
           }
+#ifdef FK_TRACE
+          if (tt == tbeg && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][5] += gtimer() - tr_sw0;
+#endif
           advance();
         }
         pos = seg_hi;
@@ -396,8 +519,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
           do {
             preb += nb;
             ++b;
-            len = seq_len<LAYOUT>(p, b, &tok0);
+            len = nlen;
+            tok0 = ntok0;
             nb = (len + PAGE - 1) / PAGE;
+            nlen = (b + 1 < p.B) ? seq_len<LAYOUT>(p, b + 1, &ntok0) : 0;
           } while (nb == 0 && b + 1 < p.B);
         }
         item_base = KVH * preb + static_cast<long long>(h) * nb;
@@ -413,6 +538,109 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
     return;
   }
 
+  if (warp > CWARPS) {
+    // ================================================================ epilogue
+    // Merge the four consumer warps' states of each finished segment; write
+    // whole items to `out`, split items to the workspace, and let the CTA
+    // that completes a split item merge its segments (CTA order: the result
+    // is deterministic) and re-arm its arrival counter.
+    const int et = threadIdx.x - (CWARPS + 1) * 32;  // 0 .. ETHREADS-1
+    const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
+    int eb = 0;
+    uint32_t eph = 0;
+    while (true) {
+      if (!mbar_wait(smem_u32(&efull[eb]), eph)) {
+        if (et == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
+        break;
+      }
+      const Meta mt = emeta[eb];
+      if (mt.flags & F_END) break;
+      const EpiSlot& E = eslot[eb];
+      const bool whole = (mt.flags & F_WHOLE) != 0;
+      const long long item = static_cast<long long>(mt.b) * p.kv_heads + mt.h;
+      const long long obase = static_cast<long long>(mt.b) * p.o_sb;
+      for (int hd = 0; hd < p.G; ++hd) {
+        float M = NEG_INF;
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, E.cm[w][hd]);
+        float ew[CWARPS], L = 0.f;
+#pragma unroll
+        for (int w = 0; w < CWARPS; ++w) {
+          ew[w] = (M == NEG_INF) ? 0.f : exp2f(E.cm[w][hd] - M);
+          L += ew[w] * E.cl[w][hd];
+        }
+        const int qh = mt.h * p.G + hd;
+#pragma unroll
+        for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) {
+          const int d = et + dd * ETHREADS;
+          float A = 0.f;
+#pragma unroll
+          for (int w = 0; w < CWARPS; ++w) A += ew[w] * E.cacc[w][hd][d];
+          if (whole) {
+            store_out(p, obase + static_cast<long long>(qh) * p.o_sh + d, finalize(A, L, M, p.s_aux, qh, sv));
+          } else {
+            ws_acc[(static_cast<long long>(mt.seg) * GPAD + hd) * HEAD_DIM + d] = A;
+          }
+        }
+        if (!whole && et == 0) ws_ml[static_cast<long long>(mt.seg) * GPAD + hd] = make_float2(M, L);
+      }
+      // the slot is consumed: give it back to the consumers
+      mbar_arrive(smem_u32(&eempty[eb]));
+      eb ^= 1;
+      if (eb == 0) eph ^= 1u;
+      if (whole) continue;
+      __threadfence();
+      named_bar_sync(2, ETHREADS);
+      if (et == 0) s_last = (atomicAdd(&cnt[item], 1) == mt.nseg - 1) ? 1 : 0;
+      named_bar_sync(2, ETHREADS);
+      if (!s_last) continue;
+      __threadfence();
+      for (int hd = 0; hd < p.G; ++hd) {
+        float M = NEG_INF, L = 0.f;
+        float A[HEAD_DIM / ETHREADS];
+#pragma unroll
+        for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) A[dd] = 0.f;
+        // blocks of 4 segments: all loads of a block are in flight together
+        for (int c = 0; c < mt.nseg; c += 4) {
+          float2 ml[4];
+          float av[4][HEAD_DIM / ETHREADS];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const long long sg = item + mt.c0 + c + u;
+            const bool ok = c + u < mt.nseg;
+            ml[u] = ok ? __ldcg(&ws_ml[sg * GPAD + hd]) : make_float2(NEG_INF, 0.f);
+#pragma unroll
+            for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd)
+              av[u][dd] = ok ? __ldcg(&ws_acc[(sg * GPAD + hd) * HEAD_DIM + et + dd * ETHREADS]) : 0.f;
+          }
+          float Mn = M;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, ml[u].x);
+          if (Mn == NEG_INF) continue;
+          const float sc = exp2f(M - Mn);
+          L *= sc;
+#pragma unroll
+          for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) A[dd] *= sc;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float e = exp2f(ml[u].x - Mn);
+            L += e * ml[u].y;
+#pragma unroll
+            for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) A[dd] += e * av[u][dd];
+          }
+          M = Mn;
+        }
+        const int qh = mt.h * p.G + hd;
+#pragma unroll
+        for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd)
+          store_out(p, obase + static_cast<long long>(qh) * p.o_sh + et + dd * ETHREADS,
+                    finalize(A[dd], L, M, p.s_aux, qh, sv));
+      }
+      if (et == 0) cnt[item] = 0;
+    }
+    return;
+  }
+
   // ================================================================ consumers
   constexpr bool FP8 = C::FP8;
   constexpr bool MBF16 = C::BF16;  // MMA element type (FP8 KV computes in f16)
@@ -420,8 +648,6 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
   const int t = lane & 3;
   const int r0 = warp * 16;
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
-  const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
-  const float sq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
 
   // Sequences of length 0 own no granules: CTA b % S writes their zero rows.
@@ -437,6 +663,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
   uint32_t qb[8][2];
   int stage = 0;
   uint32_t phase = 0;
+  int eb = 0;            // epilogue slot
+  uint32_t ephase = 0;
 
   // Thread-constant shared-memory offsets.
   const int lr = lane & 7, lq = lane >> 3;
@@ -449,20 +677,40 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
   const int cg = (g >> 1) | ((g & 1) << 2);
 
   while (true) {
+#ifdef FK_TRACE
+    const unsigned long long tw0 = gtimer();
+#endif
     if (!mbar_wait(smem_u32(&full[stage]), phase)) {
       if (lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
       break;
     }
     const Meta mt = meta[stage];
-    if (mt.flags & F_END) break;
+    if (mt.flags & F_END) {
+      // tell the epilogue warps to finish
+      if (mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u)) {
+        if (warp == 0 && lane == 0) emeta[eb].flags = F_END;
+        mbar_arrive(smem_u32(&efull[eb]));
+      } else if (lane == 0) {
+        atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
+      }
+      break;
+    }
+#ifdef FK_TRACE
+    if (threadIdx.x == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][(mt.flags & F_FIRST) ? 7 : 8] += gtimer() - tw0;
+    if (tr_first && threadIdx.x == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][1] = gtimer();
+    tr_first = false;
+    ++tr_ntile;
+    if (mt.flags & F_LAST) ++tr_nseg;
+#endif
 
     if (mt.flags & F_FIRST) {
       m[0] = m[1] = NEG_INF;
       l[0] = l[1] = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-      const bool hv = g < p.G;
-      const long long qbase = static_cast<long long>(mt.b) * p.q_sb + static_cast<long long>(mt.h * p.G + g) * p.q_sh;
+      // the producer staged this item's Q rows (MMA type, zero-padded to 8
+      // heads) next to the segment's first tile
+      const uint32_t* qrow = qstage + stage * (GPAD * 64) + g * 64;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         int d0, d1;
@@ -473,15 +721,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
           d0 = 16 * j + 2 * t;
           d1 = d0 + 8;
         }
-        float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-        if (hv) {
-          x0 = load_q_elem(p, qbase + d0, sq);
-          x1 = load_q_elem(p, qbase + d0 + 1, sq);
-          x2 = load_q_elem(p, qbase + d1, sq);
-          x3 = load_q_elem(p, qbase + d1 + 1, sq);
-        }
-        qb[j][0] = pack2<MBF16>(x0, x1);
-        qb[j][1] = pack2<MBF16>(x2, x3);
+        qb[j][0] = qrow[d0 >> 1];
+        qb[j][1] = qrow[d1 >> 1];
       }
     }
 
@@ -516,13 +757,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
       } else {
         rowA = r0 + g;
         rowB = r0 + g + 8;
-        const uint32_t kb = sK + krow * 128;
+        using TL = TileLayout<KV, LAYOUT>;
+        const uint32_t kb = sK + TL::row_off(krow);
         const int ksw = krow & 7;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int c = ((j & 3) << 1) + (lq >> 1);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4(kb + (j >> 2) * C::HALF_BYTES + ((c ^ ksw) << 4), a0, a1, a2, a3);
+          ldsm_x4(kb + (j >> 2) * TL::HALF_STRIDE + ((c ^ ksw) << 4), a0, a1, a2, a3);
           mma16816<MBF16>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
         }
       }
@@ -588,13 +830,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
           mk01 = (tok_ok(tk) ? 0x0000ffffu : 0u) | (tok_ok(tk + 1) ? 0xffff0000u : 0u);
           mk89 = (tok_ok(tk + 8) ? 0x0000ffffu : 0u) | (tok_ok(tk + 9) ? 0xffff0000u : 0u);
         }
-        const uint32_t vb = sV + vrow * 128;
+        using TL = TileLayout<KV, LAYOUT>;
+        const uint32_t vb = sV + TL::row_off(vrow);
         const int vsw = vrow & 7;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int c = ((2 * i) & 7) + (lq & 1);
           uint32_t a0, a1, a2, a3;
-          ldsm_x4_t(vb + (i >> 2) * C::HALF_BYTES + ((c ^ vsw) << 4), a0, a1, a2, a3);
+          ldsm_x4_t(vb + (i >> 2) * TL::HALF_STRIDE + ((c ^ vsw) << 4), a0, a1, a2, a3);
           mma16816<MBF16>(acc[i], a0 & mk01, a1 & mk01, a2 & mk89, a3 & mk89, pb0, pb1);
         }
       }
@@ -603,17 +846,22 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
     if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
 
     if (mt.flags & F_LAST) {
-      // ---- merge the four warps' states for this segment
+      // ---- hand this segment's state to the epilogue warps and go on
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
         l[0] += __shfl_xor_sync(0xffffffffu, l[0], o);
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], o);
       }
+      if (!mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u)) {
+        if (lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
+        break;
+      }
+      EpiSlot& E = eslot[eb];
       if (g == 0) {
-        cm[warp * GPAD + 2 * t] = m[0];
-        cm[warp * GPAD + 2 * t + 1] = m[1];
-        cl[warp * GPAD + 2 * t] = l[0];
-        cl[warp * GPAD + 2 * t + 1] = l[1];
+        E.cm[warp][2 * t] = m[0];
+        E.cm[warp][2 * t + 1] = m[1];
+        E.cl[warp][2 * t] = l[0];
+        E.cl[warp][2 * t + 1] = l[1];
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -621,76 +869,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_split_kernel(const __grid_c
         for (int r = 0; r < 2; ++r) {
           const int d = FP8 ? (16 * cg + 2 * i + r) : (16 * i + g + 8 * r);
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int hd = 2 * t + j;
-            if (hd < p.G) cacc[(warp * GPAD + hd) * HEAD_DIM + d] = acc[i][2 * r + j];
-          }
+          for (int j = 0; j < 2; ++j) E.cacc[warp][2 * t + j][d] = acc[i][2 * r + j];
         }
       }
-      named_bar_sync(1, CWARPS * 32);
-      const int d = threadIdx.x;  // 0..127
-      const bool whole = (mt.flags & F_WHOLE) != 0;
-      const long long item = static_cast<long long>(mt.b) * p.kv_heads + mt.h;
-      for (int hd = 0; hd < p.G; ++hd) {
-        float M = NEG_INF;
-#pragma unroll
-        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, cm[w * GPAD + hd]);
-        float A = 0.f, L = 0.f;
-        if (M != NEG_INF) {
-#pragma unroll
-          for (int w = 0; w < CWARPS; ++w) {
-            const float e = exp2f(cm[w * GPAD + hd] - M);
-            A += e * cacc[(w * GPAD + hd) * HEAD_DIM + d];
-            L += e * cl[w * GPAD + hd];
-          }
-        }
-        if (whole) {
-          const int qh = mt.h * p.G + hd;
-          store_out(p, static_cast<long long>(mt.b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d,
-                    finalize(A, L, M, p.s_aux, qh, sv));
-        } else {
-          ws_acc[(static_cast<long long>(mt.seg) * GPAD + hd) * HEAD_DIM + d] = A;
-          if (d == 0) ws_ml[static_cast<long long>(mt.seg) * GPAD + hd] = make_float2(M, L);
-        }
-      }
-      if (!whole) {
-        // Publish this segment; the CTA that completes the item merges all
-        // of its segments (in CTA order, so the result is deterministic) and
-        // re-arms the counter for the next launch.
-        __threadfence();
-        named_bar_sync(1, CWARPS * 32);
-        if (threadIdx.x == 0) s_last = (atomicAdd(&cnt[item], 1) == mt.nseg - 1) ? 1 : 0;
-        named_bar_sync(1, CWARPS * 32);
-        if (s_last) {
-          __threadfence();
-          for (int hd = 0; hd < p.G; ++hd) {
-            float M = NEG_INF;
-            for (int c = 0; c < mt.nseg; ++c)
-              M = fmaxf(M, __ldcg(&ws_ml[(item + mt.c0 + c) * GPAD + hd]).x);
-            float A = 0.f, L = 0.f;
-            if (M != NEG_INF) {
-              for (int c = 0; c < mt.nseg; ++c) {
-                const long long sg = item + mt.c0 + c;
-                const float2 ml = __ldcg(&ws_ml[sg * GPAD + hd]);
-                const float e = exp2f(ml.x - M);
-                A += e * __ldcg(&ws_acc[(sg * GPAD + hd) * HEAD_DIM + d]);
-                L += e * ml.y;
-              }
-            }
-            const int qh = mt.h * p.G + hd;
-            store_out(p, static_cast<long long>(mt.b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d,
-                      finalize(A, L, M, p.s_aux, qh, sv));
-          }
-          if (threadIdx.x == 0) cnt[item] = 0;
-        }
-      }
-      named_bar_sync(1, CWARPS * 32);
+      if (warp == 0 && lane == 0) emeta[eb] = mt;
+      mbar_arrive(smem_u32(&efull[eb]));
+      eb ^= 1;
+      if (eb == 0) ephase ^= 1u;
     }
     if (++stage == C::STAGES) {
       stage = 0;
       phase ^= 1u;
     }
   }
+#ifdef FK_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 4096) {
+    g_trace[blockIdx.x][2] = gtimer();
+    g_trace[blockIdx.x][3] = tr_nseg;
+    g_trace[blockIdx.x][4] = tr_ntile;
+  }
+#endif
 }
 
 // ------------------------------------------------------------------------
@@ -742,8 +940,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int KV>
 constexpr size_t smem_bytes() {
   using C = KvCfg<KV>;
-  return 1024 + C::STAGES * C::STAGE_BYTES + sizeof(float) * (CWARPS * GPAD * HEAD_DIM + 2 * CWARPS * GPAD) +
-         sizeof(Meta) * C::STAGES + 2 * sizeof(uint64_t) * C::STAGES;
+  return 1024 + C::STAGES * C::STAGE_BYTES + sizeof(Meta) * C::STAGES + sizeof(uint32_t) * C::STAGES * GPAD * 64 + 2 * sizeof(uint64_t) * C::STAGES +
+         2 * (sizeof(EpiSlot) + sizeof(Meta)) + 4 * sizeof(uint64_t);
 }
 
 template <int KV, int LAYOUT>
@@ -903,6 +1101,14 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   return rc;
 }
 
+// Q is read as element pairs (32-bit words for 16-bit Q, 16-bit for e4m3).
+int check_q_align(const void* q, int q_dtype, int64_t sq_b, int64_t sq_h) {
+  const uintptr_t a = (q_dtype == FK_DTYPE_E4M3) ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(q) % a) != 0 || (sq_b & 1) || (sq_h & 1))
+    return fail(FK_ERR_INVALID_ARG, "q must be %d-byte aligned with even batch/head strides", static_cast<int>(a));
+  return FK_OK;
+}
+
 void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out, int64_t so_b, int64_t so_h,
                  const float* s_aux, int batch, int q_heads, int kv_heads, int q_dtype, int out_dtype,
                  const float* scale_q, const float* scale_k, const float* scale_v, void* ws) {
@@ -960,6 +1166,7 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
                          workspace, &device);
   if (rc == FK_EMPTY) return FK_OK;
   if (rc != FK_OK) return rc;
+  if ((rc = check_q_align(q, dtype, sq_b, sq_h)) != FK_OK) return rc;
   if (!is16(dtype)) return fail(FK_ERR_UNSUPPORTED, "varlen decode takes f16 or bf16 tensors");
   if (cu_seqlens_k == nullptr) return fail(FK_ERR_INVALID_ARG, "cu_seqlens_k must be non-null");
   if (total_tokens < 0 || total_tokens > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad total_tokens");
@@ -994,6 +1201,7 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
                          workspace, &device);
   if (rc == FK_EMPTY) return FK_OK;
   if (rc != FK_OK) return rc;
+  if ((rc = check_q_align(q, q_dtype, sq_b, sq_h)) != FK_OK) return rc;
   if (cache_lens == nullptr) return fail(FK_ERR_INVALID_ARG, "cache_lens must be non-null");
   if (max_seqlen <= 0 || max_seqlen > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad max_seqlen");
   const int es = (kv_dtype == FK_DTYPE_E4M3) ? 1 : 2;
@@ -1033,6 +1241,7 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
                          workspace, &device);
   if (rc == FK_EMPTY) return FK_OK;
   if (rc != FK_OK) return rc;
+  if ((rc = check_q_align(q, q_dtype, sq_b, sq_h)) != FK_OK) return rc;
   if (page_size != PAGE) return fail(FK_ERR_UNSUPPORTED, "page_size must be 16 (got %d)", page_size);
   if (block_table == nullptr || seq_lens == nullptr)
     return fail(FK_ERR_INVALID_ARG, "block_table and seq_lens must be non-null");
@@ -1041,6 +1250,7 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   const int es = (kv_dtype == FK_DTYPE_E4M3) ? 1 : 2;
   if (((sk_p | sk_h | sk_s | sv_p | sv_h | sv_s) * es) % 16 != 0)
     return fail(FK_ERR_INVALID_ARG, "k/v pool strides must be multiples of 16 bytes");
+  if (num_pages > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "num_pages too large");
   Params p;
   memset(&p, 0, sizeof(p));
   fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, q_dtype, out_dtype, scale_q,
@@ -1050,15 +1260,27 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   p.bt_sb = bt_b;
   p.max_blocks = max_blocks;
   p.num_pages = static_cast<int>(num_pages);
-  const uint32_t bd = (kv_dtype == FK_DTYPE_E4M3) ? 128 : 64;
-  const uint64_t dims[4] = {HEAD_DIM, PAGE, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
-  const uint32_t box[4] = {bd, PAGE, 1, 1};
-  const uint64_t ks[3] = {static_cast<uint64_t>(sk_s) * es, static_cast<uint64_t>(sk_h) * es,
-                          static_cast<uint64_t>(sk_p) * es};
-  const uint64_t vs[3] = {static_cast<uint64_t>(sv_s) * es, static_cast<uint64_t>(sv_h) * es,
-                          static_cast<uint64_t>(sv_p) * es};
-  if ((rc = encode_map(&p.tk, kv_dtype, 4, k_pool, dims, ks, box)) != FK_OK) return rc;
-  if ((rc = encode_map(&p.tv, kv_dtype, 4, v_pool, dims, vs, box)) != FK_OK) return rc;
+  if (kv_dtype == FK_DTYPE_E4M3) {
+    // [P, KVH, 16, 128] bytes: one 16 x 128 box per page-head
+    const uint64_t dims[4] = {HEAD_DIM, PAGE, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
+    const uint32_t box[4] = {128, PAGE, 1, 1};
+    const uint64_t ks[3] = {static_cast<uint64_t>(sk_s), static_cast<uint64_t>(sk_h), static_cast<uint64_t>(sk_p)};
+    const uint64_t vs[3] = {static_cast<uint64_t>(sv_s), static_cast<uint64_t>(sv_h), static_cast<uint64_t>(sv_p)};
+    if ((rc = encode_map(&p.tk, kv_dtype, 4, k_pool, dims, ks, box)) != FK_OK) return rc;
+    if ((rc = encode_map(&p.tv, kv_dtype, 4, v_pool, dims, vs, box)) != FK_OK) return rc;
+  } else {
+    // 16-bit: the head dim is split into (64 dims, 2 halves); the half index is
+    // the third dimension (stride 128 B), so one box {64, 16, 2} carries a whole
+    // page-head and lands as [half][16 rows][64 dims] in shared memory.
+    const uint64_t dims[5] = {64, PAGE, 2, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
+    const uint32_t box[5] = {64, PAGE, 2, 1, 1};
+    const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
+                            static_cast<uint64_t>(sk_p) * 2};
+    const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
+                            static_cast<uint64_t>(sv_p) * 2};
+    if ((rc = encode_map(&p.tk, kv_dtype, 5, k_pool, dims, ks, box)) != FK_OK) return rc;
+    if ((rc = encode_map(&p.tv, kv_dtype, 5, v_pool, dims, vs, box)) != FK_OK) return rc;
+  }
   return launch<PAGED>(p, kv_dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -1185,3 +1407,9 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
                                     head_dim, total_tokens, dtype, sq_b, sq_h, sk_t, sk_h, sv_t, sv_h, so_b, so_h,
                                     scratch, NOALLOC_SCRATCH_BYTES, stream);
 }
+
+#ifdef FK_TRACE
+extern "C" int fk_trace_read(unsigned long long* host, int n) {
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 10 * n) == cudaSuccess ? 0 : 1;
+}
+#endif

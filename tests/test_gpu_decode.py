@@ -298,3 +298,25 @@ def test_config3_full_size_paged_equals_varlen(dev):
         ref = O.decode_varlen(d["q"][b:b + 1].float().cpu().numpy(), d["k"][lo:hi].float().cpu().numpy(),
                               d["v"][lo:hi].float().cpu().numpy(), np.array([0, hi - lo]))
         close(outp[b:b + 1], ref, **F16_TOL)
+
+
+def test_config4_full_size_fp8_paged_equals_dense(dev):
+    lens = W.config_lengths(4)
+    d = W.make_varlen(lens, 32, 8, torch.float16, dev, seed=0, sinks=True)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.0, seed=0)
+    kp, vp = kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    outp = fk.paged_flash_decode(d["q"], kp, vp, bt, sl, 16, s_aux=d["s_aux"], scale_k=sk, scale_v=sv)
+    kc = k8.view(16, 32768, 8, 128).transpose(1, 2)  # [B, KVH, S, D] strided view of the same bytes
+    vc = v8.view(16, 32768, 8, 128).transpose(1, 2)
+    outd = fk.flash_decode_gqa_hf_fp8(d["q"], kc, vc, sl, None, sk, sv, torch.float16, s_aux=d["s_aux"])
+    assert torch.equal(outp, outd)
+    for b in (0, 15):
+        lo, hi = b * 32768, (b + 1) * 32768
+        ref = O.decode_varlen(d["q"][b:b + 1].float().cpu().numpy(), (k8[lo:hi].float() * sk).cpu().numpy(),
+                              (v8[lo:hi].float() * sv).cpu().numpy(), np.array([0, 32768]),
+                              d["s_aux"].cpu().numpy())
+        close(outp[b:b + 1], ref, **FP8_TOL)
+    assert N.read_status(dev) == 0
