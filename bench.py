@@ -159,6 +159,30 @@ def setup_workload(name, rank, world, device):
                "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
         return dict(run=run, q=q, lens_dev=sl, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 2), cfg=cfg,
                     scaling="weak", sample=None, dtype="fp16 in / fp32 accumulate")
+    if name == "config4d":  # config 4 on the HF dense BHSD cache (flash_decode_gqa_hf_fp8 path)
+        spec = W.CONFIGS[4]
+        lens = W.config_lengths(4, seed=rank)
+        B, S = spec.batch, lens[0]
+        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
+        k8, sk = W.quantize_e4m3(d["k"])
+        del d["k"]
+        v8, sv = W.quantize_e4m3(d["v"])
+        del d["v"]
+        kc = k8.view(B, S, spec.kv_heads, 128).transpose(1, 2).contiguous()
+        vc = v8.view(B, S, spec.kv_heads, 128).transpose(1, 2).contiguous()
+        del k8, v8
+        q, s = d["q"], d["s_aux"]
+        cl = torch.tensor(lens, dtype=torch.int32, device=device)
+        out = torch.empty_like(q)
+
+        def run(qq=q, ll=cl, oo=out):
+            return fk.flash_decode_gqa_hf_fp8(qq, kc, vc, ll, None, sk, sv, torch.float16, s_aux=s, out=oo)
+        cfg = {"workload": spec.name + "_hf_dense", "batch_per_gpu": B, "global_batch": B * world,
+               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128, "seq_lens": "32768 all",
+               "kv_layout": "HF dense [B, KV_H, S, D] e4m3 KV (per-tensor scale), fp16 Q", "sinks": True,
+               "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
+        return dict(run=run, q=q, lens_dev=cl, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 1), cfg=cfg,
+                    scaling="weak", sample=None, dtype="e4m3 KV / fp16 Q / fp32 accumulate")
     if name == "config4":
         spec = W.CONFIGS[4]
         lens = W.config_lengths(4, seed=rank)
@@ -371,7 +395,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     from oracle import gqa_decode_oracle as O
-    if args.workload in ("config3", "config3v", "config4", "config5"):
+    if args.workload in ("config3", "config3v", "config4", "config4d", "config5"):
         spec = W.CONFIGS[int(args.workload[6])]
         lens = W.config_lengths(spec, seed=0)
         kvh, qh, es = spec.kv_heads, spec.q_heads, (1 if spec.kv_dtype == torch.float8_e4m3fn else 2)
@@ -411,7 +435,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["config2", "config2s", "config3", "config3v", "config4", "config5"], default="config2")
+    ap.add_argument("--workload", choices=["config2", "config2s", "config3", "config3v", "config4", "config4d", "config5"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -72,7 +72,8 @@ struct KvCfg {
   static constexpr int ES = FP8 ? 1 : 2;                     // bytes per element
   static constexpr int TILE_BYTES = TILE * HEAD_DIM * ES;    // K (or V) bytes per stage
   static constexpr int PAGE_BYTES = PAGE * HEAD_DIM * ES;    // one page of K (or V)
-  static constexpr int STAGES = FP8 ? 4 : 5;
+  static constexpr int STAGES = 5;
+  static constexpr int NSLOT = FP8 ? 1 : 2;                  // epilogue slots (smem budget: 2 CTAs/SM for FP8)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int BOX_D = FP8 ? 128 : 64;               // dims per TMA box (128 bytes)
   static constexpr int NHALF = HEAD_DIM / BOX_D;             // boxes per 128-dim row
@@ -266,13 +267,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* stages = smem;
   EpiSlot* eslot = reinterpret_cast<EpiSlot*>(smem + C::STAGES * C::STAGE_BYTES);  // [2]
-  Meta* emeta = reinterpret_cast<Meta*>(eslot + 2);                                  // [2]
-  Meta* meta = emeta + 2;                                                            // [STAGES]
+  Meta* emeta = reinterpret_cast<Meta*>(eslot + C::NSLOT);                            // [NSLOT]
+  Meta* meta = emeta + C::NSLOT;                                                           // [STAGES]
   uint32_t* qstage = reinterpret_cast<uint32_t*>(meta + C::STAGES);                 // [STAGES][GPAD*64] (f16x2/bf16x2)
   uint64_t* full = reinterpret_cast<uint64_t*>(qstage + C::STAGES * GPAD * 64);     // [STAGES]
   uint64_t* empty = full + C::STAGES;                                               // [STAGES]
   uint64_t* efull = empty + C::STAGES;                                              // [2]
-  uint64_t* eempty = efull + 2;                                                     // [2]
+  uint64_t* eempty = efull + C::NSLOT;                                              // [NSLOT]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), CWARPS);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::NSLOT; ++s) {
       mbar_init(smem_u32(&efull[s]), CWARPS * 32);
       mbar_init(smem_u32(&eempty[s]), ETHREADS);
     }
@@ -586,8 +587,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       }
       // the slot is consumed: give it back to the consumers
       mbar_arrive(smem_u32(&eempty[eb]));
-      eb ^= 1;
-      if (eb == 0) eph ^= 1u;
+      if (++eb == C::NSLOT) {
+        eb = 0;
+        eph ^= 1u;
+      }
       if (whole) continue;
       __threadfence();
       named_bar_sync(2, ETHREADS);
@@ -734,6 +737,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 
       // ---- S^T = K Q^T : 16 tokens x 8 heads
       float s[4] = {0.f, 0.f, 0.f, 0.f};
+      float s2[4] = {0.f, 0.f, 0.f, 0.f};  // odd k-steps: two independent MMA chains
       int rowA, rowB;
       if constexpr (FP8) {
         rowA = prow;
@@ -752,7 +756,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           const uint32_t a2 = e4m3x2_to_f16x2(wa[j] >> 16);
           const uint32_t a1 = e4m3x2_to_f16x2(wb[j]);
           const uint32_t a3 = e4m3x2_to_f16x2(wb[j] >> 16);
-          mma16816<false>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
+          if (j & 1) mma16816<false>(s2, a0, a1, a2, a3, qb[j][0], qb[j][1]);
+          else mma16816<false>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
         }
       } else {
         rowA = r0 + g;
@@ -765,10 +770,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           const int c = ((j & 3) << 1) + (lq >> 1);
           uint32_t a0, a1, a2, a3;
           ldsm_x4(kb + (j >> 2) * TL::HALF_STRIDE + ((c ^ ksw) << 4), a0, a1, a2, a3);
-          mma16816<MBF16>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
+          if (j & 1) mma16816<MBF16>(s2, a0, a1, a2, a3, qb[j][0], qb[j][1]);
+          else mma16816<MBF16>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
         }
       }
 
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[i] += s2[i];
       // ---- online softmax (log2 domain), heads 2t and 2t+1
       const bool okA = tok_ok(rowA), okB = tok_ok(rowB);
       const float x0 = okA ? s[0] * qk_scale : NEG_INF;
@@ -874,8 +882,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       }
       if (warp == 0 && lane == 0) emeta[eb] = mt;
       mbar_arrive(smem_u32(&efull[eb]));
-      eb ^= 1;
-      if (eb == 0) ephase ^= 1u;
+      if (++eb == C::NSLOT) {
+        eb = 0;
+        ephase ^= 1u;
+      }
     }
     if (++stage == C::STAGES) {
       stage = 0;
@@ -941,7 +951,7 @@ template <int KV>
 constexpr size_t smem_bytes() {
   using C = KvCfg<KV>;
   return 1024 + C::STAGES * C::STAGE_BYTES + sizeof(Meta) * C::STAGES + sizeof(uint32_t) * C::STAGES * GPAD * 64 + 2 * sizeof(uint64_t) * C::STAGES +
-         2 * (sizeof(EpiSlot) + sizeof(Meta)) + 4 * sizeof(uint64_t);
+         C::NSLOT * (sizeof(EpiSlot) + sizeof(Meta) + 2 * sizeof(uint64_t));
 }
 
 template <int KV, int LAYOUT>
