@@ -82,7 +82,7 @@ def lib() -> ctypes.CDLL:
         L.fk_profile_end.restype = _I
         L.fk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I)]
         L.fk_decode_num_ctas.restype = _I
-        L.fk_decode_num_ctas.argtypes = [_I, _I]
+        L.fk_decode_num_ctas.argtypes = [_I, _I, _I]
         _lib = L
         return L
 

@@ -40,6 +40,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -56,6 +57,8 @@ constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
 constexpr int EWARPS = 2;      // epilogue warps: segment merge / output / partials
 constexpr int THREADS = (CWARPS + 1 + EWARPS) * 32;
 constexpr int ETHREADS = EWARPS * 32;
+constexpr int HPMAX = 2;       // KV heads per work item (2 when kv_heads is even)
+constexpr int GMAX = HPMAX * 8; // query-head slots per segment record
 constexpr int PAGE = 16;       // tokens per granule (= page size)
 constexpr int MIN_PER = 4;
 constexpr int FK_EMPTY = -1;  // internal: common_checks found an empty batch     // minimum granules per CTA (one tile)
@@ -72,7 +75,7 @@ struct KvCfg {
   static constexpr int ES = FP8 ? 1 : 2;                     // bytes per element
   static constexpr int TILE_BYTES = TILE * HEAD_DIM * ES;    // K (or V) bytes per stage
   static constexpr int PAGE_BYTES = PAGE * HEAD_DIM * ES;    // one page of K (or V)
-  static constexpr int STAGES = 5;
+  static constexpr int STAGES = FP8 ? 4 : 5;
   static constexpr int NSLOT = FP8 ? 1 : 2;                  // epilogue slots (smem budget: 2 CTAs/SM for FP8)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int BOX_D = FP8 ? 128 : 64;               // dims per TMA box (128 bytes)
@@ -89,19 +92,30 @@ struct EpiSlot {
   float cacc[CWARPS][GPAD][HEAD_DIM];
 };
 
-// Shared-memory tile layouts of a 64-token K (or V) stage, 128-byte swizzled
-// (16-byte chunk index XOR row & 7).  16-bit KV stores two 64-dim halves:
-//   VARLEN / DENSE: [half][64 rows][64 dims]      (one 8 KB TMA box per half)
-//   PAGED:          [page][half][16 rows][64 dims] (one 4 KB TMA box per page)
-// FP8 KV stores [64 rows][128 dims] for every layout.  Row r, 16-byte chunk c
-// of the 256-byte (16-bit) row is at row_off(r) + (c >> 3) * half_stride +
-// (((c & 7) ^ (r & 7)) << 4).
-template <int KV, int LAYOUT>
+// Shared-memory tile layouts of one K (or V) stage: TT = 64/HP tokens of each
+// of the item's HP KV heads, 128-byte swizzled (16-byte chunk index XOR
+// row & 7).  A 16-bit row is 256 bytes, stored as two 64-dim halves.
+//   16-bit VARLEN / DENSE: [head][half][TT rows][64 dims]   one TMA box per stage
+//   16-bit PAGED:          [page][head][half][16][64 dims]  one TMA box per page
+//   e4m3 VARLEN / DENSE:   [head][TT rows][128 dims]
+//   e4m3 PAGED:            [page][head][16][128 dims]
+// Row r of head hh, 16-byte chunk c is at row_off(hh, r) + (c >> 3) *
+// HALF_STRIDE + (((c & 7) ^ (r & 7)) << 4) (e4m3: c < 8).  All bases are
+// multiples of 1024 bytes, so the swizzle line of row r is r & 7 everywhere.
+template <int KV, int LAYOUT, int HP>
 struct TileLayout {
-  static constexpr bool GROUPED = (LAYOUT == 2 /* PAGED */) && KV != FK_DTYPE_E4M3;
-  static constexpr uint32_t HALF_STRIDE = GROUPED ? 2048u : uint32_t(TILE * 128);
-  __device__ static __forceinline__ uint32_t row_off(int r) {
-    return GROUPED ? uint32_t((r >> 4) * 4096 + (r & 15) * 128) : uint32_t(r * 128);
+  static constexpr bool FP8 = KV == FK_DTYPE_E4M3;
+  static constexpr bool PG = LAYOUT == 2;  // PAGED
+  static constexpr int TT = TILE / HP;
+  static constexpr uint32_t HALF_STRIDE = PG ? 2048u : uint32_t(TT * 128);
+  __device__ static __forceinline__ uint32_t row_off(int hh, int r) {
+    if constexpr (FP8) {
+      if constexpr (PG) return uint32_t((r >> 4) * (HP * 2048) + hh * 2048 + (r & 15) * 128);
+      else return uint32_t(hh * (TT * 128) + r * 128);
+    } else {
+      if constexpr (PG) return uint32_t((r >> 4) * (HP * 4096) + hh * 4096 + (r & 15) * 128);
+      else return uint32_t(hh * (2 * TT * 128) + r * 128);
+    }
   }
 };
 
@@ -114,8 +128,8 @@ struct Meta {
 //   [0, 256)                 header (status word)
 //   [256, 256 + 4*cap)       cnt[cap]: per-item arrival counters, cap =
 //                            (W - 256) / SEG_BYTES; zero between launches
-//   ml  (aligned 256)        float2[(S+I)*8]  segment (max, sum)
-//   acc (aligned 256)        float[(S+I)*8*128] segment accumulators
+//   ml  (aligned 256)        float2[(S+I)*16]  segment (max, sum) per query-head slot
+//   acc (aligned 256)        float[(S+I)*16*128] segment accumulators
 // A launch with I = B*KVH items fits when I <= cap and acc + its size <= W.
 // Partials of one launch can therefore never overwrite the counters another
 // launch (of any shape) uses on the same buffer.
@@ -125,7 +139,7 @@ struct WsHeader {
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-constexpr size_t SEG_BYTES = 4 + GPAD * sizeof(float2) + GPAD * HEAD_DIM * sizeof(float);  // per segment (+1 counter)
+constexpr size_t SEG_BYTES = 4 + GMAX * sizeof(float2) + GMAX * HEAD_DIM * sizeof(float);  // per segment (+1 counter)
 
 struct WsLayout {
   size_t cap, cnt, ml, acc, need;
@@ -134,8 +148,8 @@ struct WsLayout {
     cap = W > 256 ? (W - 256) / SEG_BYTES : 0;
     cnt = 256;
     ml = align_up(cnt + 4 * cap, 256);
-    acc = align_up(ml + segs * GPAD * sizeof(float2), 256);
-    need = acc + segs * GPAD * HEAD_DIM * sizeof(float);
+    acc = align_up(ml + segs * GMAX * sizeof(float2), 256);
+    need = acc + segs * GMAX * HEAD_DIM * sizeof(float);
   }
   bool fits(size_t W, int B, int kvh) const { return static_cast<size_t>(B) * kvh <= cap && need <= W; }
   // Smallest buffer size whose own layout fits (B, kvh, S).
@@ -260,20 +274,25 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // ------------------------------------------------------------------------
 // Split pass.
 // ------------------------------------------------------------------------
-template <int KV, int LAYOUT>
+template <int KV, int LAYOUT, int HP>
 __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
   using C = KvCfg<KV>;
+  using TL = TileLayout<KV, LAYOUT, HP>;
+  constexpr int TT = TILE / HP;          // tokens per KV head in one stage
+  constexpr int WPH = CWARPS / HP;       // consumer warps per KV head
+  constexpr int PPT = TT / PAGE;         // pages per KV head in one stage
+  constexpr int QWORDS = HP * GPAD * 64; // staged Q words per stage
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* stages = smem;
-  EpiSlot* eslot = reinterpret_cast<EpiSlot*>(smem + C::STAGES * C::STAGE_BYTES);  // [2]
-  Meta* emeta = reinterpret_cast<Meta*>(eslot + C::NSLOT);                            // [NSLOT]
-  Meta* meta = emeta + C::NSLOT;                                                           // [STAGES]
-  uint32_t* qstage = reinterpret_cast<uint32_t*>(meta + C::STAGES);                 // [STAGES][GPAD*64] (f16x2/bf16x2)
-  uint64_t* full = reinterpret_cast<uint64_t*>(qstage + C::STAGES * GPAD * 64);     // [STAGES]
-  uint64_t* empty = full + C::STAGES;                                               // [STAGES]
-  uint64_t* efull = empty + C::STAGES;                                              // [2]
-  uint64_t* eempty = efull + C::NSLOT;                                              // [NSLOT]
+  EpiSlot* eslot = reinterpret_cast<EpiSlot*>(smem + C::STAGES * C::STAGE_BYTES);  // [NSLOT]
+  Meta* emeta = reinterpret_cast<Meta*>(eslot + C::NSLOT);                         // [NSLOT]
+  Meta* meta = emeta + C::NSLOT;                                                   // [STAGES]
+  uint32_t* qstage = reinterpret_cast<uint32_t*>(meta + C::STAGES);                // [STAGES][QWORDS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(qstage + C::STAGES * QWORDS);       // [STAGES]
+  uint64_t* empty = full + C::STAGES;                                              // [STAGES]
+  uint64_t* efull = empty + C::STAGES;                                             // [NSLOT]
+  uint64_t* eempty = efull + C::NSLOT;                                             // [NSLOT]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -281,6 +300,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   int* cnt = reinterpret_cast<int*>(p.ws + p.ws_cnt);
   float2* ws_ml = reinterpret_cast<float2*>(p.ws + p.ws_ml);
   float* ws_acc = reinterpret_cast<float*>(p.ws + p.ws_acc);
+  const int KVI = p.kv_heads / HP;  // items per sequence
   __shared__ int s_last;
 
 #ifdef FK_TRACE
@@ -310,7 +330,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       prefetch_tmap(&p.tk);
       prefetch_tmap(&p.tv);
     }
-    const long long KVH = p.kv_heads;
+    const long long NI = KVI;
     const float psq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
     // Plan: total granules of the whole batch.
     long long tot = 0;
@@ -322,7 +342,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
       tot += n;
     }
-    const long long U = tot * KVH;
+    const long long U = tot * NI;
     const long long S = p.num_ctas;
     const long long per = max((U + S - 1) / S, static_cast<long long>(MIN_PER));
     const long long start = static_cast<long long>(blockIdx.x) * per;
@@ -361,7 +381,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         long long t0;
         const long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
         const long long inc = warp_incl_scan(n, lane);
-        const bool hit = (b < p.B) && (KVH * (run + inc) > start);
+        const bool hit = (b < p.B) && (NI * (run + inc) > start);
         const unsigned m = __ballot_sync(0xffffffffu, hit);
         if (m) {
           const int L = __ffs(m) - 1;
@@ -374,25 +394,26 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       long long tok0;
       int len = seq_len<LAYOUT>(p, b, &tok0);
       long long nb = (len + PAGE - 1) / PAGE;
-      int h = static_cast<int>((start - KVH * preb) / nb);
-      long long item_base = KVH * preb + static_cast<long long>(h) * nb;
+      int hi = static_cast<int>((start - NI * preb) / nb);  // item head index (KV heads hi*HP ..)
+      long long item_base = NI * preb + static_cast<long long>(hi) * nb;
       long long pos = start;
 
-      // Q words of the next item, prefetched into registers (lane owns words
-      // lane + 32k of the [8 heads][64 pairs] block).
-      constexpr int QW = GPAD * 64 / 32;
+      // Q words of the next item, prefetched into registers: lane owns words
+      // lane + 32k of the [HP][8 heads][64 pairs] block.
+      constexpr int QW = HP * GPAD * 64 / 32;
       uint32_t qpre[QW];
       int qpre_b = -1, qpre_h = -1;
-      auto q_prefetch = [&](int bb, int hh) {
+      auto q_prefetch = [&](int bb, int ih) {
         const long long qb0 = static_cast<long long>(bb) * p.q_sb;
 #pragma unroll
         for (int k = 0; k < QW; ++k) {
           const int idx = lane + 32 * k;
-          const int j = idx >> 6, d = (idx & 63) * 2;
-          qpre[k] = (j < p.G) ? load_q_pair_raw(p, qb0 + static_cast<long long>(hh * p.G + j) * p.q_sh + d) : 0u;
+          const int hh = idx / (GPAD * 64), j = (idx >> 6) & (GPAD - 1), d = (idx & 63) * 2;
+          const int qh = (ih * HP + hh) * p.G + j;
+          qpre[k] = (j < p.G) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d) : 0u;
         }
         qpre_b = bb;
-        qpre_h = hh;
+        qpre_h = ih;
       };
       // length of the next sequence, prefetched
       long long ntok0 = 0;
@@ -411,16 +432,17 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         const int g0 = static_cast<int>(pos - item_base);
         const int g1 = static_cast<int>(seg_hi - item_base);
         const bool whole = (item_base >= start) && (item_base + nb <= end);
-        const int seg = blockIdx.x + b * p.kv_heads + h;
+        const int seg = blockIdx.x + b * KVI + hi;
         const int c0 = static_cast<int>(item_base / per);
         const int nseg = static_cast<int>((item_base + nb - 1) / per) - c0 + 1;
         const int tbeg = g0 * PAGE;
         const int tend = min(g1 * PAGE, len);
+        const int hcoord = hi * HP;  // first KV head of the item
 #ifdef FK_TRACE
         unsigned long long tr_sw0 = gtimer();
 #endif
-        for (int tt = tbeg; tt < tend; tt += TILE) {
-          const int valid = min(TILE, tend - tt);
+        for (int tt = tbeg; tt < tend; tt += TT) {
+          const int valid = min(TT, tend - tt);
           if (!acquire()) {
             alive = false;
             break;
@@ -431,11 +453,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           int bad = 0;
           uint32_t bytes = 2u * C::TILE_BYTES;
           int phys = -1;
-          int np = 0;
           if constexpr (LAYOUT == PAGED) {
             const int p0 = tt / PAGE;
-            np = (valid + PAGE - 1) / PAGE;
-            if (b != win_b || p0 < win_p0 || p0 + 4 > win_p0 + 32) {
+            const int np = (valid + PAGE - 1) / PAGE;
+            if (b != win_b || p0 < win_p0 || p0 + PPT > win_p0 + 32) {
               if (b == win_b && p0 == win_p0 + 32) {
                 bt_cur = bt_nxt;
                 win_p0 += 32;
@@ -446,23 +467,23 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
               }
               bt_nxt = ld_bt(b, win_p0 + 32 + lane);
             }
-            phys = __shfl_sync(0xffffffffu, bt_cur, (p0 - win_p0) + (lane & 3));
+            phys = __shfl_sync(0xffffffffu, bt_cur, (p0 - win_p0) + (lane & (PPT - 1)));
             const bool okp = (lane < np) && phys >= 0 && phys < p.num_pages;
-            const unsigned okm = __ballot_sync(0xffffffffu, okp) & 0xfu;
+            const unsigned okm = __ballot_sync(0xffffffffu, okp) & ((1u << PPT) - 1u);
             bad = static_cast<int>(~okm & ((1u << np) - 1u));
-            bytes = static_cast<uint32_t>(__popc(okm)) * 2u * C::PAGE_BYTES;
+            bytes = static_cast<uint32_t>(__popc(okm)) * 2u * HP * C::PAGE_BYTES;
             if (lane == 0 && bad) atomicOr(&hdr->status, FK_STATUS_BAD_PAGE);
             if (!okp) phys = -1;
           }
           if (tt == tbeg) {
-            // Q rows of item (b, h) -> qstage[stage] as packed MMA-type pairs,
+            // Q rows of the item -> qstage[stage] as packed MMA-type pairs,
             // from the registers prefetched one item ahead
-            if (qpre_b != b || qpre_h != h) q_prefetch(b, h);
-            uint32_t* qs = qstage + stage * (GPAD * 64);
+            if (qpre_b != b || qpre_h != hi) q_prefetch(b, hi);
+            uint32_t* qs = qstage + stage * QWORDS;
 #pragma unroll
             for (int k = 0; k < QW; ++k) qs[lane + 32 * k] = q_pair_to_mma<C::BF16>(p, qpre[k], psq);
             // start fetching the next item's Q
-            if (h + 1 < p.kv_heads) q_prefetch(b, h + 1);
+            if (hi + 1 < KVI) q_prefetch(b, hi + 1);
             else if (b + 1 < p.B) q_prefetch(b + 1, 0);
             __threadfence_block();
             __syncwarp();
@@ -470,10 +491,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           if (lane == 0) {
             Meta& mt = meta[stage];
             mt.b = b;
-            mt.h = h;
+            mt.h = hi;
             mt.tok = tt;
             mt.valid = valid;
-            mt.flags = (tt == tbeg ? F_FIRST : 0) | (tt + TILE >= tend ? F_LAST : 0) | (whole ? F_WHOLE : 0);
+            mt.flags = (tt == tbeg ? F_FIRST : 0) | (tt + TT >= tend ? F_LAST : 0) | (whole ? F_WHOLE : 0);
             mt.seg = seg;
             mt.bad = bad;
             mt.c0 = c0;
@@ -483,28 +504,34 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           __syncwarp();
           if constexpr (LAYOUT == PAGED) {
             if (phys >= 0) {
-              // one box per page-head: 16 tokens x 128 dims
-              const uint32_t off = lane * (PAGE * 128 * C::ES);
+              // one box per page: 16 tokens x HP heads x 128 dims
+              const uint32_t off = lane * (HP * PAGE * 128 * C::ES);
               if constexpr (C::FP8) {
-                tma_load_4d(sK + off, &p.tk, fb, 0, 0, h, phys);
-                tma_load_4d(sV + off, &p.tv, fb, 0, 0, h, phys);
+                tma_load_4d(sK + off, &p.tk, fb, 0, 0, hcoord, phys);
+                tma_load_4d(sV + off, &p.tv, fb, 0, 0, hcoord, phys);
               } else {
-                tma_load_5d(sK + off, &p.tk, fb, 0, 0, 0, h, phys);
-                tma_load_5d(sV + off, &p.tv, fb, 0, 0, 0, h, phys);
+                tma_load_5d(sK + off, &p.tk, fb, 0, 0, 0, hcoord, phys);
+                tma_load_5d(sV + off, &p.tv, fb, 0, 0, 0, hcoord, phys);
               }
             }
           } else if (lane == 0) {
-#pragma unroll
-            for (int hf = 0; hf < C::NHALF; ++hf) {
-              const uint32_t off = hf * C::HALF_BYTES;
-              if constexpr (LAYOUT == VARLEN) {
-                const int row = static_cast<int>(tok0 + tt);
-                tma_load_3d(sK + off, &p.tk, fb, hf * C::BOX_D, h, row);
-                tma_load_3d(sV + off, &p.tv, fb, hf * C::BOX_D, h, row);
+            // one box per stage: TT tokens x HP heads x 128 dims
+            const int row = static_cast<int>(tok0 + tt);
+            if constexpr (LAYOUT == VARLEN) {
+              if constexpr (C::FP8) {
+                tma_load_3d(sK, &p.tk, fb, 0, row, hcoord);
+                tma_load_3d(sV, &p.tv, fb, 0, row, hcoord);
               } else {
-                const int row = static_cast<int>(tok0 + tt);
-                tma_load_4d(sK + off, &p.tk, fb, hf * C::BOX_D, row, h, b);
-                tma_load_4d(sV + off, &p.tv, fb, hf * C::BOX_D, row, h, b);
+                tma_load_4d(sK, &p.tk, fb, 0, row, 0, hcoord);
+                tma_load_4d(sV, &p.tv, fb, 0, row, 0, hcoord);
+              }
+            } else {
+              if constexpr (C::FP8) {
+                tma_load_4d(sK, &p.tk, fb, 0, row, hcoord, b);
+                tma_load_4d(sV, &p.tv, fb, 0, row, hcoord, b);
+              } else {
+                tma_load_5d(sK, &p.tk, fb, 0, row, 0, hcoord, b);
+                tma_load_5d(sV, &p.tv, fb, 0, row, 0, hcoord, b);
               }
             }
           }
@@ -515,8 +542,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         }
         pos = seg_hi;
         if (pos >= end) break;
-        if (++h == p.kv_heads) {
-          h = 0;
+        if (++hi == KVI) {
+          hi = 0;
           do {
             preb += nb;
             ++b;
@@ -526,7 +553,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
             nlen = (b + 1 < p.B) ? seq_len<LAYOUT>(p, b + 1, &ntok0) : 0;
           } while (nb == 0 && b + 1 < p.B);
         }
-        item_base = KVH * preb + static_cast<long long>(h) * nb;
+        item_base = NI * preb + static_cast<long long>(hi) * nb;
       }
     }
     // End-of-work marker.
@@ -541,12 +568,14 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 
   if (warp > CWARPS) {
     // ================================================================ epilogue
-    // Merge the four consumer warps' states of each finished segment; write
-    // whole items to `out`, split items to the workspace, and let the CTA
-    // that completes a split item merge its segments (CTA order: the result
-    // is deterministic) and re-arm its arrival counter.
+    // Merge the consumer warps' states of each finished segment (per KV head:
+    // its WPH warps); write whole items to `out`, split items to the
+    // workspace, and let the CTA that completes a split item merge its
+    // segments (CTA order: the result is deterministic) and re-arm its
+    // arrival counter.
     const int et = threadIdx.x - (CWARPS + 1) * 32;  // 0 .. ETHREADS-1
     const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
+    constexpr int DPT = HEAD_DIM / ETHREADS;           // dims per epilogue thread
     int eb = 0;
     uint32_t eph = 0;
     while (true) {
@@ -558,32 +587,35 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       if (mt.flags & F_END) break;
       const EpiSlot& E = eslot[eb];
       const bool whole = (mt.flags & F_WHOLE) != 0;
-      const long long item = static_cast<long long>(mt.b) * p.kv_heads + mt.h;
+      const long long item = static_cast<long long>(mt.b) * KVI + mt.h;
       const long long obase = static_cast<long long>(mt.b) * p.o_sb;
-      for (int hd = 0; hd < p.G; ++hd) {
-        float M = NEG_INF;
 #pragma unroll
-        for (int w = 0; w < CWARPS; ++w) M = fmaxf(M, E.cm[w][hd]);
-        float ew[CWARPS], L = 0.f;
+      for (int hh = 0; hh < HP; ++hh) {
+        for (int hd = 0; hd < p.G; ++hd) {
+          float M = NEG_INF;
 #pragma unroll
-        for (int w = 0; w < CWARPS; ++w) {
-          ew[w] = (M == NEG_INF) ? 0.f : exp2f(E.cm[w][hd] - M);
-          L += ew[w] * E.cl[w][hd];
-        }
-        const int qh = mt.h * p.G + hd;
+          for (int w = 0; w < WPH; ++w) M = fmaxf(M, E.cm[hh * WPH + w][hd]);
+          float ew[WPH], L = 0.f;
 #pragma unroll
-        for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) {
-          const int d = et + dd * ETHREADS;
-          float A = 0.f;
-#pragma unroll
-          for (int w = 0; w < CWARPS; ++w) A += ew[w] * E.cacc[w][hd][d];
-          if (whole) {
-            store_out(p, obase + static_cast<long long>(qh) * p.o_sh + d, finalize(A, L, M, p.s_aux, qh, sv));
-          } else {
-            ws_acc[(static_cast<long long>(mt.seg) * GPAD + hd) * HEAD_DIM + d] = A;
+          for (int w = 0; w < WPH; ++w) {
+            ew[w] = (M == NEG_INF) ? 0.f : exp2f(E.cm[hh * WPH + w][hd] - M);
+            L += ew[w] * E.cl[hh * WPH + w][hd];
           }
+          const int qh = (mt.h * HP + hh) * p.G + hd;
+          const int hs = hh * GPAD + hd;  // head slot in a segment record
+#pragma unroll
+          for (int dd = 0; dd < DPT; ++dd) {
+            const int d = et + dd * ETHREADS;
+            float A = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPH; ++w) A += ew[w] * E.cacc[hh * WPH + w][hd][d];
+            if (whole)
+              store_out(p, obase + static_cast<long long>(qh) * p.o_sh + d, finalize(A, L, M, p.s_aux, qh, sv));
+            else
+              ws_acc[(static_cast<long long>(mt.seg) * GMAX + hs) * HEAD_DIM + d] = A;
+          }
+          if (!whole && et == 0) ws_ml[static_cast<long long>(mt.seg) * GMAX + hs] = make_float2(M, L);
         }
-        if (!whole && et == 0) ws_ml[static_cast<long long>(mt.seg) * GPAD + hd] = make_float2(M, L);
       }
       // the slot is consumed: give it back to the consumers
       mbar_arrive(smem_u32(&eempty[eb]));
@@ -598,46 +630,53 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       named_bar_sync(2, ETHREADS);
       if (!s_last) continue;
       __threadfence();
-      for (int hd = 0; hd < p.G; ++hd) {
+      // All head slots in parallel: unit u = (slot u / 8, dims (u % 8) * 16 ..
+      // +16); each thread merges its units with 4 segments' loads in flight.
+      for (int u = et; u < HP * p.G * 8; u += ETHREADS) {
+        const int hh = u / (p.G * 8), hd = (u / 8) % p.G, d0 = (u % 8) * 16;
+        const int hs = hh * GPAD + hd;
         float M = NEG_INF, L = 0.f;
-        float A[HEAD_DIM / ETHREADS];
+        float A[16];
 #pragma unroll
-        for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) A[dd] = 0.f;
-        // blocks of 4 segments: all loads of a block are in flight together
+        for (int i = 0; i < 16; ++i) A[i] = 0.f;
         for (int c = 0; c < mt.nseg; c += 4) {
           float2 ml[4];
-          float av[4][HEAD_DIM / ETHREADS];
+          float4 av[4][4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const long long sg = item + mt.c0 + c + u;
-            const bool ok = c + u < mt.nseg;
-            ml[u] = ok ? __ldcg(&ws_ml[sg * GPAD + hd]) : make_float2(NEG_INF, 0.f);
+          for (int v = 0; v < 4; ++v) {
+            const long long sg = item + mt.c0 + c + v;
+            const bool ok = c + v < mt.nseg;
+            ml[v] = ok ? __ldcg(&ws_ml[sg * GMAX + hs]) : make_float2(NEG_INF, 0.f);
+            const float4* src = reinterpret_cast<const float4*>(&ws_acc[(sg * GMAX + hs) * HEAD_DIM + d0]);
 #pragma unroll
-            for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd)
-              av[u][dd] = ok ? __ldcg(&ws_acc[(sg * GPAD + hd) * HEAD_DIM + et + dd * ETHREADS]) : 0.f;
+            for (int i = 0; i < 4; ++i) av[v][i] = ok ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
           float Mn = M;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) Mn = fmaxf(Mn, ml[u].x);
+          for (int v = 0; v < 4; ++v) Mn = fmaxf(Mn, ml[v].x);
           if (Mn == NEG_INF) continue;
           const float sc = exp2f(M - Mn);
           L *= sc;
 #pragma unroll
-          for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) A[dd] *= sc;
+          for (int i = 0; i < 16; ++i) A[i] *= sc;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float e = exp2f(ml[u].x - Mn);
-            L += e * ml[u].y;
+          for (int v = 0; v < 4; ++v) {
+            const float e = exp2f(ml[v].x - Mn);
+            L += e * ml[v].y;
 #pragma unroll
-            for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd) A[dd] += e * av[u][dd];
+            for (int i = 0; i < 4; ++i) {
+              A[4 * i + 0] += e * av[v][i].x;
+              A[4 * i + 1] += e * av[v][i].y;
+              A[4 * i + 2] += e * av[v][i].z;
+              A[4 * i + 3] += e * av[v][i].w;
+            }
           }
           M = Mn;
         }
-        const int qh = mt.h * p.G + hd;
+        const int qh = (mt.h * HP + hh) * p.G + hd;
+        const long long ob = obase + static_cast<long long>(qh) * p.o_sh + d0;
 #pragma unroll
-        for (int dd = 0; dd < HEAD_DIM / ETHREADS; ++dd)
-          store_out(p, obase + static_cast<long long>(qh) * p.o_sh + et + dd * ETHREADS,
-                    finalize(A[dd], L, M, p.s_aux, qh, sv));
+        for (int i = 0; i < 16; ++i) store_out(p, ob + i, finalize(A[i], L, M, p.s_aux, qh, sv));
       }
       if (et == 0) cnt[item] = 0;
     }
@@ -649,7 +688,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   constexpr bool MBF16 = C::BF16;  // MMA element type (FP8 KV computes in f16)
   const int g = lane >> 2;
   const int t = lane & 3;
-  const int r0 = warp * 16;
+  const int hh = warp / WPH;            // KV head of the item this warp serves
+  const int r0 = (warp % WPH) * 16;      // its 16 rows of that head's tile
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
 
@@ -713,7 +753,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
       // the producer staged this item's Q rows (MMA type, zero-padded to 8
       // heads) next to the segment's first tile
-      const uint32_t* qrow = qstage + stage * (GPAD * 64) + g * 64;
+      const uint32_t* qrow = qstage + stage * QWORDS + hh * (GPAD * 64) + g * 64;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         int d0, d1;
@@ -743,7 +783,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         rowA = prow;
         rowB = prow + 8;
         const int sw = prow & 7;
-        const uint32_t ra = sK + prow * 128, rb = ra + 8 * 128;
+        const uint32_t ra = sK + TL::row_off(hh, prow), rb = ra + 8 * 128;
         const uint4 alo = lds128(ra + ((t ^ sw) << 4));
         const uint4 ahi = lds128(ra + (((t + 4) ^ sw) << 4));
         const uint4 blo = lds128(rb + ((t ^ sw) << 4));
@@ -762,8 +802,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       } else {
         rowA = r0 + g;
         rowB = r0 + g + 8;
-        using TL = TileLayout<KV, LAYOUT>;
-        const uint32_t kb = sK + TL::row_off(krow);
+        const uint32_t kb = sK + TL::row_off(hh, krow);
         const int ksw = krow & 7;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -816,7 +855,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const int row = r0 + t + 4 * (r & 1) + 8 * (r >> 1);
-          x[r] = lds128(sV + row * 128 + ((cg ^ (row & 7)) << 4));
+          x[r] = lds128(sV + TL::row_off(hh, row) + ((cg ^ (row & 7)) << 4));
           if (partial && !tok_ok(row)) x[r] = make_uint4(0u, 0u, 0u, 0u);
         }
         const uint32_t w0[4] = {x[0].x, x[0].y, x[0].z, x[0].w};
@@ -838,8 +877,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           mk01 = (tok_ok(tk) ? 0x0000ffffu : 0u) | (tok_ok(tk + 1) ? 0xffff0000u : 0u);
           mk89 = (tok_ok(tk + 8) ? 0x0000ffffu : 0u) | (tok_ok(tk + 9) ? 0xffff0000u : 0u);
         }
-        using TL = TileLayout<KV, LAYOUT>;
-        const uint32_t vb = sV + TL::row_off(vrow);
+        const uint32_t vb = sV + TL::row_off(hh, vrow);
         const int vsw = vrow & 7;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -947,69 +985,77 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-template <int KV>
+template <int KV, int HP>
 constexpr size_t smem_bytes() {
   using C = KvCfg<KV>;
-  return 1024 + C::STAGES * C::STAGE_BYTES + sizeof(Meta) * C::STAGES + sizeof(uint32_t) * C::STAGES * GPAD * 64 + 2 * sizeof(uint64_t) * C::STAGES +
+  return 1024 + C::STAGES * (C::STAGE_BYTES + sizeof(Meta) + sizeof(uint32_t) * HP * GPAD * 64 + 2 * sizeof(uint64_t)) +
          C::NSLOT * (sizeof(EpiSlot) + sizeof(Meta) + 2 * sizeof(uint64_t));
 }
 
-template <int KV, int LAYOUT>
+// KV heads per work item: 2 when kv_heads is even (one TMA box then covers
+// both heads of a page), else 1.  FK_DECODE_HP=1 in the environment forces
+// single-head items (a tuning knob; read once, applies to every layout so
+// paged and contiguous results stay bit-identical).
+inline int hp_for(int kv_heads) {
+  static const int forced = [] {
+    const char* e = getenv("FK_DECODE_HP");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
+  if (forced == 1) return 1;
+  return (kv_heads % 2 == 0) ? 2 : 1;
+}
+
+template <int KV, int LAYOUT, int HP>
 int prepare_kernel(int device) {
   static bool done[64] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lk(mu);
   if (device < 0 || device >= 64) return fail(FK_ERR_INVALID_ARG, "device index %d out of range", device);
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_bytes<KV>()));
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_bytes<KV, HP>()));
     if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done[device] = true;
   }
   return FK_OK;
 }
 
-// Resident CTAs of the split kernel on `device` for KV type `kv`: the
-// persistent grid size S.  It depends on the KV type only (the three layout
-// instantiations share the shared-memory footprint and launch bounds), so
-// paged and contiguous calls plan identical segments.
-int num_work_ctas(int device, int kv) {
-  static int cache[64][3] = {};
+template <int KV, int HP>
+int occupancy(int device, int* per_sm) {
+  int rc = prepare_kernel<KV, VARLEN, HP>(device);
+  if (rc != FK_OK) return rc;
+  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, decode_split_kernel<KV, VARLEN, HP>,
+                                                                      THREADS, smem_bytes<KV, HP>());
+  return e == cudaSuccess ? FK_OK : fail(FK_ERR_CUDA, "occupancy query failed: %s", cudaGetErrorString(e));
+}
+
+// Resident CTAs of the decode kernel on `device` for KV type `kv` and HP KV
+// heads per item: the persistent grid size S.  It does not depend on the
+// layout (the layout instantiations share shared-memory footprint and launch
+// bounds), so paged, dense and varlen calls plan identical segments.
+int num_work_ctas(int device, int kv, int hp) {
+  static int cache[64][3][2] = {};
   static std::mutex mu;
-  if (device < 0 || device >= 64 || kv < 0 || kv > 2) return 0;
+  if (device < 0 || device >= 64 || kv < 0 || kv > 2 || hp < 1 || hp > 2) return 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (cache[device][kv] > 0) return cache[device][kv];
+    if (cache[device][kv][hp - 1] > 0) return cache[device][kv][hp - 1];
   }
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
-  int per_sm = 0;
-  cudaError_t e = cudaSuccess;
-  int prev = 0;
+  int per_sm = 0, prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
-  switch (kv) {
-    case FK_DTYPE_F16:
-      if (prepare_kernel<FK_DTYPE_F16, VARLEN>(device) != FK_OK) break;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<FK_DTYPE_F16, VARLEN>, THREADS,
-                                                        smem_bytes<FK_DTYPE_F16>());
-      break;
-    case FK_DTYPE_BF16:
-      if (prepare_kernel<FK_DTYPE_BF16, VARLEN>(device) != FK_OK) break;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<FK_DTYPE_BF16, VARLEN>,
-                                                        THREADS, smem_bytes<FK_DTYPE_BF16>());
-      break;
-    default:
-      if (prepare_kernel<FK_DTYPE_E4M3, VARLEN>(device) != FK_OK) break;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_split_kernel<FK_DTYPE_E4M3, VARLEN>,
-                                                        THREADS, smem_bytes<FK_DTYPE_E4M3>());
-      break;
-  }
+  int rc;
+  if (kv == FK_DTYPE_F16) rc = hp == 2 ? occupancy<FK_DTYPE_F16, 2>(device, &per_sm) : occupancy<FK_DTYPE_F16, 1>(device, &per_sm);
+  else if (kv == FK_DTYPE_BF16) rc = hp == 2 ? occupancy<FK_DTYPE_BF16, 2>(device, &per_sm) : occupancy<FK_DTYPE_BF16, 1>(device, &per_sm);
+  else rc = hp == 2 ? occupancy<FK_DTYPE_E4M3, 2>(device, &per_sm) : occupancy<FK_DTYPE_E4M3, 1>(device, &per_sm);
   if (prev != device) cudaSetDevice(prev);
-  if (e != cudaSuccess || per_sm <= 0) return 0;
+  if (rc != FK_OK || per_sm <= 0) return 0;
   std::lock_guard<std::mutex> lk(mu);
-  cache[device][kv] = sms * per_sm;
-  return cache[device][kv];
+  cache[device][kv][hp - 1] = sms * per_sm;
+  return cache[device][kv][hp - 1];
 }
 
 int encode_map(CUtensorMap* map, int kv, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_b,
@@ -1067,9 +1113,17 @@ int common_checks(const void* q, const void* k, const void* v, const void* out, 
   return FK_OK;
 }
 
+template <int KV, int LAYOUT, int HP>
+int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
+  const int rc = prepare_kernel<KV, LAYOUT, HP>(device);
+  if (rc == FK_OK) decode_split_kernel<KV, LAYOUT, HP><<<S, THREADS, smem_bytes<KV, HP>(), stream>>>(p);
+  return rc;
+}
+
 template <int LAYOUT>
 int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) {
-  const int S = num_work_ctas(device, kv);
+  const int hp = hp_for(p.kv_heads);
+  const int S = num_work_ctas(device, kv, hp);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   p.num_ctas = S;
   const WsLayout wl(ws_bytes, p.B, p.kv_heads, S);
@@ -1083,25 +1137,14 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   int prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
-  int rc = FK_OK;
   prof_mark(0, stream);
-  switch (kv) {
-    case FK_DTYPE_F16:
-      rc = prepare_kernel<FK_DTYPE_F16, LAYOUT>(device);
-      if (rc == FK_OK)
-        decode_split_kernel<FK_DTYPE_F16, LAYOUT><<<S, THREADS, smem_bytes<FK_DTYPE_F16>(), stream>>>(p);
-      break;
-    case FK_DTYPE_BF16:
-      rc = prepare_kernel<FK_DTYPE_BF16, LAYOUT>(device);
-      if (rc == FK_OK)
-        decode_split_kernel<FK_DTYPE_BF16, LAYOUT><<<S, THREADS, smem_bytes<FK_DTYPE_BF16>(), stream>>>(p);
-      break;
-    default:
-      rc = prepare_kernel<FK_DTYPE_E4M3, LAYOUT>(device);
-      if (rc == FK_OK)
-        decode_split_kernel<FK_DTYPE_E4M3, LAYOUT><<<S, THREADS, smem_bytes<FK_DTYPE_E4M3>(), stream>>>(p);
-      break;
-  }
+  int rc;
+  if (kv == FK_DTYPE_F16)
+    rc = hp == 2 ? launch_one<FK_DTYPE_F16, LAYOUT, 2>(p, S, device, stream) : launch_one<FK_DTYPE_F16, LAYOUT, 1>(p, S, device, stream);
+  else if (kv == FK_DTYPE_BF16)
+    rc = hp == 2 ? launch_one<FK_DTYPE_BF16, LAYOUT, 2>(p, S, device, stream) : launch_one<FK_DTYPE_BF16, LAYOUT, 1>(p, S, device, stream);
+  else
+    rc = hp == 2 ? launch_one<FK_DTYPE_E4M3, LAYOUT, 2>(p, S, device, stream) : launch_one<FK_DTYPE_E4M3, LAYOUT, 1>(p, S, device, stream);
   if (rc == FK_OK) {
     prof_mark(1, stream);
     const cudaError_t e = cudaGetLastError();
@@ -1157,7 +1200,7 @@ extern "C" size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads,
     fail(FK_ERR_INVALID_ARG, "bad sizes");
     return 0;
   }
-  const int S = num_work_ctas(device, kv_dtype);
+  const int S = num_work_ctas(device, kv_dtype, hp_for(kv_heads));
   if (S <= 0) {
     fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
     return 0;
@@ -1188,12 +1231,15 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
               nullptr, workspace);
   p.lens = cu_seqlens_k;
   const uint64_t T = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
-  const uint64_t dims[3] = {HEAD_DIM, static_cast<uint64_t>(kv_heads), T};
-  const uint32_t box[3] = {64, 1, TILE};
-  const uint64_t ks[2] = {static_cast<uint64_t>(sk_h) * 2, static_cast<uint64_t>(sk_t) * 2};
-  const uint64_t vs[2] = {static_cast<uint64_t>(sv_h) * 2, static_cast<uint64_t>(sv_t) * 2};
-  if ((rc = encode_map(&p.tk, dtype, 3, k_varlen, dims, ks, box)) != FK_OK) return rc;
-  if ((rc = encode_map(&p.tv, dtype, 3, v_varlen, dims, vs, box)) != FK_OK) return rc;
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads));
+  // 16-bit rows as (64 dims, T rows, 2 halves [128 B apart], heads): one box
+  // {64, 64/hp, 2, hp} per stage lands as [head][half][rows][64].
+  const uint64_t dims[4] = {64, T, 2, static_cast<uint64_t>(kv_heads)};
+  const uint32_t box[4] = {64, TILE / hp, 2, hp};
+  const uint64_t ks[3] = {static_cast<uint64_t>(sk_t) * 2, 128, static_cast<uint64_t>(sk_h) * 2};
+  const uint64_t vs[3] = {static_cast<uint64_t>(sv_t) * 2, 128, static_cast<uint64_t>(sv_h) * 2};
+  if ((rc = encode_map(&p.tk, dtype, 4, k_varlen, dims, ks, box)) != FK_OK) return rc;
+  if ((rc = encode_map(&p.tv, dtype, 4, v_varlen, dims, vs, box)) != FK_OK) return rc;
   return launch<VARLEN>(p, dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -1224,16 +1270,27 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
   p.lens = cache_lens;
   p.starts = start_k_offsets;
   p.max_tokens = max_seqlen;
-  const uint32_t bd = (kv_dtype == FK_DTYPE_E4M3) ? 128 : 64;
-  const uint64_t dims[4] = {HEAD_DIM, static_cast<uint64_t>(max_seqlen), static_cast<uint64_t>(kv_heads),
-                            static_cast<uint64_t>(batch > 0 ? batch : 1)};
-  const uint32_t box[4] = {bd, TILE, 1, 1};
-  const uint64_t ks[3] = {static_cast<uint64_t>(sk_s) * es, static_cast<uint64_t>(sk_h) * es,
-                          static_cast<uint64_t>(sk_b) * es};
-  const uint64_t vs[3] = {static_cast<uint64_t>(sv_s) * es, static_cast<uint64_t>(sv_h) * es,
-                          static_cast<uint64_t>(sv_b) * es};
-  if ((rc = encode_map(&p.tk, kv_dtype, 4, k_cache, dims, ks, box)) != FK_OK) return rc;
-  if ((rc = encode_map(&p.tv, kv_dtype, 4, v_cache, dims, vs, box)) != FK_OK) return rc;
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads));
+  const uint64_t Bd = static_cast<uint64_t>(batch > 0 ? batch : 1);
+  if (kv_dtype == FK_DTYPE_E4M3) {
+    // (128 dims, S rows, heads, batch): box {128, 64/hp, hp, 1} -> [head][rows][128]
+    const uint64_t dims[4] = {HEAD_DIM, static_cast<uint64_t>(max_seqlen), static_cast<uint64_t>(kv_heads), Bd};
+    const uint32_t box[4] = {128, TILE / hp, hp, 1};
+    const uint64_t ks[3] = {static_cast<uint64_t>(sk_s), static_cast<uint64_t>(sk_h), static_cast<uint64_t>(sk_b)};
+    const uint64_t vs[3] = {static_cast<uint64_t>(sv_s), static_cast<uint64_t>(sv_h), static_cast<uint64_t>(sv_b)};
+    if ((rc = encode_map(&p.tk, kv_dtype, 4, k_cache, dims, ks, box)) != FK_OK) return rc;
+    if ((rc = encode_map(&p.tv, kv_dtype, 4, v_cache, dims, vs, box)) != FK_OK) return rc;
+  } else {
+    // (64 dims, S rows, 2 halves, heads, batch): box {64, 64/hp, 2, hp, 1} -> [head][half][rows][64]
+    const uint64_t dims[5] = {64, static_cast<uint64_t>(max_seqlen), 2, static_cast<uint64_t>(kv_heads), Bd};
+    const uint32_t box[5] = {64, TILE / hp, 2, hp, 1};
+    const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
+                            static_cast<uint64_t>(sk_b) * 2};
+    const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
+                            static_cast<uint64_t>(sv_b) * 2};
+    if ((rc = encode_map(&p.tk, kv_dtype, 5, k_cache, dims, ks, box)) != FK_OK) return rc;
+    if ((rc = encode_map(&p.tv, kv_dtype, 5, v_cache, dims, vs, box)) != FK_OK) return rc;
+  }
   return launch<DENSE>(p, kv_dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -1270,20 +1327,21 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   p.bt_sb = bt_b;
   p.max_blocks = max_blocks;
   p.num_pages = static_cast<int>(num_pages);
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads));
   if (kv_dtype == FK_DTYPE_E4M3) {
-    // [P, KVH, 16, 128] bytes: one 16 x 128 box per page-head
+    // [P, KVH, 16, 128] bytes: one box {128, 16, hp, 1} per page -> [head][16][128]
     const uint64_t dims[4] = {HEAD_DIM, PAGE, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
-    const uint32_t box[4] = {128, PAGE, 1, 1};
+    const uint32_t box[4] = {128, PAGE, hp, 1};
     const uint64_t ks[3] = {static_cast<uint64_t>(sk_s), static_cast<uint64_t>(sk_h), static_cast<uint64_t>(sk_p)};
     const uint64_t vs[3] = {static_cast<uint64_t>(sv_s), static_cast<uint64_t>(sv_h), static_cast<uint64_t>(sv_p)};
     if ((rc = encode_map(&p.tk, kv_dtype, 4, k_pool, dims, ks, box)) != FK_OK) return rc;
     if ((rc = encode_map(&p.tv, kv_dtype, 4, v_pool, dims, vs, box)) != FK_OK) return rc;
   } else {
     // 16-bit: the head dim is split into (64 dims, 2 halves); the half index is
-    // the third dimension (stride 128 B), so one box {64, 16, 2} carries a whole
-    // page-head and lands as [half][16 rows][64 dims] in shared memory.
+    // the third dimension (stride 128 B), so one box {64, 16, 2, hp} carries a
+    // page for the item's heads and lands as [head][half][16 rows][64 dims].
     const uint64_t dims[5] = {64, PAGE, 2, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
-    const uint32_t box[5] = {64, PAGE, 2, 1, 1};
+    const uint32_t box[5] = {64, PAGE, 2, hp, 1};
     const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
                             static_cast<uint64_t>(sk_p) * 2};
     const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
@@ -1334,7 +1392,9 @@ extern "C" int fk_profile_end(float* kernel_ms, int* launches) {
   return FK_OK;
 }
 
-extern "C" int fk_decode_num_ctas(int device, int kv_dtype) { return num_work_ctas(device, kv_dtype); }
+extern "C" int fk_decode_num_ctas(int device, int kv_dtype, int kv_heads) {
+  return num_work_ctas(device, kv_dtype, hp_for(kv_heads));
+}
 
 // ==========================================================================
 // Allocation-free variant of the varlen decode.
@@ -1392,7 +1452,7 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
   }
   const int device = attr.device;
   if (batch < 0 || kv_heads <= 0) return fail(FK_ERR_INVALID_ARG, "bad sizes: batch=%d kv_heads=%d", batch, kv_heads);
-  const int S = num_work_ctas(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16);
+  const int S = num_work_ctas(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp_for(kv_heads));
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   const size_t need = WsLayout::min_bytes(batch, kv_heads, S);
   if (need > NOALLOC_SCRATCH_BYTES)

@@ -188,8 +188,9 @@ int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_varlen, cons
 /* Bytes of the fixed scratch used by fk_flash_decode_gqa_varlen_noalloc. */
 size_t fk_noalloc_scratch_bytes(void);
 
-/* Size of the persistent split-pass grid (resident CTAs) on `device`. */
-int fk_decode_num_ctas(int device, int kv_dtype);
+/* Size of the persistent decode grid (resident CTAs) on `device` for this
+ * KV element type and KV head count. */
+int fk_decode_num_ctas(int device, int kv_dtype, int kv_heads);
 
 #ifdef __cplusplus
 }

@@ -320,3 +320,15 @@ def test_config4_full_size_fp8_paged_equals_dense(dev):
                               d["s_aux"].cpu().numpy())
         close(outp[b:b + 1], ref, **FP8_TOL)
     assert N.read_status(dev) == 0
+
+
+@pytest.mark.parametrize("kvh", [1, 3])
+def test_odd_kv_heads_single_head_items(dev, kvh):
+    # odd KV head counts run one KV head per work item; paged == varlen still holds
+    lens = [1, 300, 2049, 17]
+    q, k, v, cu, s = _rand_case(dev, lens, 4 * kvh, kvh, torch.float16, True, seed=30 + kvh)
+    outv = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(outv, _oracle(q, k, v, cu, s), **F16_TOL)
+    kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.25, seed=kvh)
+    outp = fk.paged_flash_decode(q, kp, vp, bt, torch.tensor(lens, dtype=torch.int32, device=dev), 16, s_aux=s)
+    assert torch.equal(outp, outv)
