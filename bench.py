@@ -106,7 +106,7 @@ def setup_workload(name, rank, world, device):
     import fasterkernels_b200 as fk
     if name in ("config2", "config2s"):
         spec = W.CONFIGS[2]
-        lens = W.config_lengths(2, seed=rank)
+        lens = W.config_lengths(2, seed=0)
         if name == "config2s":  # profiling case: first 8 sequences (~0.4 GB of KV, still > L2)
             lens = lens[:8]
         d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
@@ -119,7 +119,7 @@ def setup_workload(name, rank, world, device):
         cfg = {"workload": spec.name + ("" if name == "config2" else "_first8"), "batch_per_gpu": len(lens),
                "global_batch": len(lens) * world,
                "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
-               "seq_lens": "U[8192,16384], seed = rank", "tokens_this_rank": int(sum(lens)),
+               "seq_lens": "U[8192,16384] seed 0 (same per-GPU work on every rank; q/k/v/s_aux seed = rank)", "tokens_this_rank": int(sum(lens)),
                "kv_layout": "contiguous varlen [T, KV_H, D] fp16", "sinks": True,
                "l2": "inputs larger than L2 (>=1.5 GB KV per GPU, no flush)",
                "parallelism": f"dp{world} (each rank its own batch, no collective)"}
@@ -127,7 +127,7 @@ def setup_workload(name, rank, world, device):
                     sample=(q, k, v, cu, s, lens), dtype="fp16 in / fp32 accumulate")
     if name == "config3v":  # config-3 lengths in the contiguous varlen layout (comparison / profiling)
         spec = W.CONFIGS[3]
-        lens = W.config_lengths(3, seed=rank)
+        lens = W.config_lengths(3, seed=0)
         d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=False)
         q, k, v, cu = d["q"], d["k"], d["v"], d["cu_seqlens"]
         out = torch.empty_like(q)
@@ -136,13 +136,13 @@ def setup_workload(name, rank, world, device):
             return fk.flash_decode_gqa_varlen(qq, k, v, cc, out=oo)
         cfg = {"workload": spec.name + "_as_varlen", "batch_per_gpu": spec.batch, "global_batch": spec.batch * world,
                "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
-               "seq_lens": "U[512,8192], seed = rank", "kv_layout": "contiguous varlen fp16", "sinks": False,
+               "seq_lens": "U[512,8192] seed 0 (same on every rank; data seed = rank)", "kv_layout": "contiguous varlen fp16", "sinks": False,
                "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
         return dict(run=run, q=q, lens_dev=cu, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 2), cfg=cfg,
                     scaling="weak", sample=None, dtype="fp16 in / fp32 accumulate")
     if name == "config3":
         spec = W.CONFIGS[3]
-        lens = W.config_lengths(3, seed=rank)
+        lens = W.config_lengths(3, seed=0)
         d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=False)
         kp, vp, bt = W.varlen_to_paged(d["k"], d["v"], lens, spec.pool_factor, seed=rank)
         del d["k"], d["v"]
@@ -154,14 +154,14 @@ def setup_workload(name, rank, world, device):
             return fk.paged_flash_decode(qq, kp, vp, bt, ll, 16, out=oo)
         cfg = {"workload": spec.name, "batch_per_gpu": spec.batch, "global_batch": spec.batch * world,
                "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
-               "seq_lens": "U[512,8192], seed = rank", "pool_pages": int(kp.shape[0]),
+               "seq_lens": "U[512,8192] seed 0 (same on every rank; data seed = rank)", "pool_pages": int(kp.shape[0]),
                "kv_layout": "paged 16-token pages (random permutation of a x1.25 pool), fp16", "sinks": False,
                "l2": "inputs larger than L2", "parallelism": f"dp{world} (each rank its own batch)"}
         return dict(run=run, q=q, lens_dev=sl, out=out, kv_bytes=W.kv_bytes(lens, spec.kv_heads, 2), cfg=cfg,
                     scaling="weak", sample=None, dtype="fp16 in / fp32 accumulate")
     if name == "config4d":  # config 4 on the HF dense BHSD cache (flash_decode_gqa_hf_fp8 path)
         spec = W.CONFIGS[4]
-        lens = W.config_lengths(4, seed=rank)
+        lens = W.config_lengths(4, seed=0)
         B, S = spec.batch, lens[0]
         d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
         k8, sk = W.quantize_e4m3(d["k"])
@@ -185,7 +185,7 @@ def setup_workload(name, rank, world, device):
                     scaling="weak", sample=None, dtype="e4m3 KV / fp16 Q / fp32 accumulate")
     if name == "config4":
         spec = W.CONFIGS[4]
-        lens = W.config_lengths(4, seed=rank)
+        lens = W.config_lengths(4, seed=0)
         d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
         k8, sk = W.quantize_e4m3(d["k"])
         del d["k"]
