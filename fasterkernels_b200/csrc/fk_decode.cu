@@ -323,6 +323,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     fence_mbar_init();
   }
   __syncthreads();
+  // Let the next decode kernel in the stream start its CTAs (planning and
+  // KV loads) as SMs free up; its epilogue warps wait for this grid.
+  grid_dependency_trigger();
 
   if (warp == CWARPS) {
     // ================================================================ producer
@@ -574,6 +577,18 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     // segments (CTA order: the result is deterministic) and re-arm its
     // arrival counter.
     const int et = threadIdx.x - (CWARPS + 1) * 32;  // 0 .. ETHREADS-1
+    // Only these warps write global memory: wait until the previous kernel
+    // in the stream (if launched as its programmatic dependent) has finished.
+    grid_dependency_wait();
+    // Sequences of length 0 own no granules: CTA b % S writes their zero rows.
+    for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
+      long long t0;
+      if (seq_len<LAYOUT>(p, b, &t0) == 0) {
+        for (int qh = 0; qh < p.q_heads; ++qh)
+          for (int d = et; d < HEAD_DIM; d += ETHREADS)
+            store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d, 0.f);
+      }
+    }
     const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
     constexpr int DPT = HEAD_DIM / ETHREADS;           // dims per epilogue thread
     int eb = 0;
@@ -692,15 +707,6 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   const int r0 = (warp % WPH) * 16;      // its 16 rows of that head's tile
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
-
-  // Sequences of length 0 own no granules: CTA b % S writes their zero rows.
-  for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-    long long t0;
-    if (seq_len<LAYOUT>(p, b, &t0) == 0) {
-      for (int qh = 0; qh < p.q_heads; ++qh)
-        store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + threadIdx.x, 0.f);
-    }
-  }
 
   float m[2], l[2], acc[8][4];
   uint32_t qb[8][2];
@@ -1113,11 +1119,33 @@ int common_checks(const void* q, const void* k, const void* v, const void* out, 
   return FK_OK;
 }
 
+// Programmatic dependent launch of consecutive decode kernels (default on;
+// FK_DECODE_PDL=0 turns it off).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FK_DECODE_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int KV, int LAYOUT, int HP>
 int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
   const int rc = prepare_kernel<KV, LAYOUT, HP>(device);
-  if (rc == FK_OK) decode_split_kernel<KV, LAYOUT, HP><<<S, THREADS, smem_bytes<KV, HP>(), stream>>>(p);
-  return rc;
+  if (rc != FK_OK) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem_bytes<KV, HP>();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP>, p);
+  if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaLaunchKernelEx: %s", cudaGetErrorString(e));
+  return FK_OK;
 }
 
 template <int LAYOUT>
@@ -1408,7 +1436,7 @@ extern "C" int fk_decode_num_ctas(int device, int kv_dtype, int kv_heads) {
 // ==========================================================================
 namespace fk {
 
-constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(8) << 20;  // 8 MiB: up to ~2000 segments
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(8) << 20;  // 8 MiB: up to ~1000 segments
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
 // Device address of g_noalloc_scratch, resolved once per device.  In host code

@@ -169,7 +169,8 @@ int fk_profile_end(float* kernel_ms, int* launches);
  * allowed once serving starts -- the scratch comes from a fixed array inside
  * the library (fk_noalloc_scratch_bytes() bytes, 8 MiB, held on every GPU that
  * loads the library until exit).  It fits batch * kv_heads + (resident CTAs)
- * <= about 2000 segments; larger calls return FK_ERR_WORKSPACE.
+ * <= about 1000 segments (about 850 sequence-head pairs for 16-bit KV);
+ * larger calls return FK_ERR_WORKSPACE.
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture.  Each call clears the scratch's
  * status word and counters on `stream`.  All calls share the one array, so

@@ -332,3 +332,26 @@ def test_odd_kv_heads_single_head_items(dev, kvh):
     kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.25, seed=kvh)
     outp = fk.paged_flash_decode(q, kp, vp, bt, torch.tensor(lens, dtype=torch.int32, device=dev), 16, s_aux=s)
     assert torch.equal(outp, outv)
+
+
+def test_back_to_back_calls_overlapping_launches(dev):
+    # consecutive decode kernels may overlap (programmatic dependent launch):
+    # later calls that reuse the workspace and the output must not be
+    # disturbed by, or disturb, the previous call
+    cases = []
+    for seed, lens in ((40, [9000, 3000, 12000]), (41, [50, 20000, 7]), (42, [4096] * 6)):
+        cases.append(_rand_case(dev, lens, 32, 8, torch.float16, True, seed=seed))
+    shared_out = torch.empty_like(cases[0][0])
+    outs = []
+    for rep in range(3):
+        for i, (q, k, v, cu, s) in enumerate(cases):
+            o = fk.flash_decode_gqa_varlen(q, k, v, cu, s, out=shared_out if i == 0 else None)
+            outs.append((i, o))
+    fk.flash_decode_gqa_varlen(*cases[0], out=shared_out)  # shared_out last written by case 0
+    torch.cuda.synchronize()
+    refs = [_oracle(*c) for c in cases]
+    close(shared_out, refs[0], **F16_TOL)
+    for i, o in outs:
+        if i != 0:
+            close(o, refs[i], **F16_TOL)
+    assert N.read_status(dev) == 0
