@@ -77,6 +77,13 @@ def lib() -> ctypes.CDLL:
             _P, _P, _P,                      # scales
             _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L,
             _P, _Z, _P]
+        L.fk_paged_kv_append.restype = _I
+        L.fk_paged_kv_append.argtypes = [
+            _P, _P, _I, _P, _P, _I, _P, _P, _I,  # k_new v_new in_dtype k_pool v_pool pool_dtype bt positions increment
+            _P, _P, _P,                          # scale_k scale_v status
+            _I, _I, _I, _L, _I,                  # batch kv_heads head_dim num_pages max_blocks
+            _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L,
+            _P]
         L.fk_profile_begin.restype = _I
         L.fk_profile_begin.argtypes = [_I]
         L.fk_profile_end.restype = _I

@@ -46,6 +46,12 @@ class PagedKVCache:
         self._pages: List[List[int]] = [[] for _ in range(self.max_seqs)]
         # popped from the end: lowest page indices are handed out last, as in the reference
         self._free_pages: List[int] = list(range(self.num_pages))
+        # e4m3 pools store x / scale; fixed per-tensor scales (set_fp8_scales)
+        self.k_scale = torch.ones((), dtype=torch.float32, device=self.device)
+        self.v_scale = torch.ones((), dtype=torch.float32, device=self.device)
+        self._step_ids: List[int] = []
+        self._step_bt = None
+        self._step_pos = None
 
     @classmethod
     def from_config(cls, config, num_pages: int = 4096, max_seqs: int = 16, max_blocks_per_seq: int = 512,
@@ -93,6 +99,58 @@ class PagedKVCache:
         self.k_pool[layer_idx, pp, :, off, :] = k[0, :, 0, :]
         self.v_pool[layer_idx, pp, :, off, :] = v[0, :, 0, :]
         self._seq_lens[seq_id] = pos + 1
+
+    def set_fp8_scales(self, k_scale, v_scale) -> None:
+        """Per-tensor scales of an e4m3 pool (value = e4m3 x scale), e.g. amax / 448
+        of calibration K/V."""
+        self.k_scale.fill_(float(k_scale))
+        self.v_scale.fill_(float(v_scale))
+
+    # ---------------------------------------------------------- batched decode step
+    def begin_step(self, seq_ids: List[int]):
+        """Reserve the slot of one new token for each sequence in ``seq_ids``:
+        pages are allocated on the host (no device read-back) and the new
+        block-table entries are written with one host-to-device copy.  Returns
+        (block_table [B, max_blocks], positions [B]) device tensors for
+        ``append_kv_batch`` and the decode call."""
+        rows, cols, vals = [], [], []
+        for sid in seq_ids:
+            pos = self._seq_lens[sid]
+            page_idx = pos // PAGE_SIZE
+            pages = self._pages[sid]
+            if page_idx == len(pages):
+                if page_idx >= self.max_blocks_per_seq:
+                    raise RuntimeError("sequence exceeds max_blocks_per_seq")
+                pp = self._alloc_page()
+                pages.append(pp)
+                rows.append(sid)
+                cols.append(page_idx)
+                vals.append(pp)
+        if rows:
+            upd = torch.tensor([rows, cols, vals], dtype=torch.int64).to(self.device, non_blocking=True)
+            self.block_table[upd[0], upd[1]] = upd[2].to(torch.int32)
+        self._step_ids = list(seq_ids)
+        self._step_bt = self.get_block_table_tensor(self._step_ids)
+        self._step_pos = self.get_seq_lens_tensor(self._step_ids)
+        return self._step_bt, self._step_pos, self._step_pos + 1
+
+    def append_kv_batch(self, layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Write this step's K/V ([B, KV_H, 128] or [B, KV_H, 1, 128]) of every
+        sequence of ``begin_step`` into layer ``layer_idx`` with one kernel."""
+        from .paged_append import paged_kv_append
+        if self._step_pos is None:
+            raise RuntimeError("call begin_step() before append_kv_batch()")
+        paged_kv_append(k, v, self.k_pool[layer_idx], self.v_pool[layer_idx], self._step_bt, self._step_pos,
+                        scale_k=self.k_scale, scale_v=self.v_scale)
+
+    def end_step(self) -> torch.Tensor:
+        """Commit the step: every sequence of ``begin_step`` grows by one token.
+        Returns the new lengths [B] (device) for the next decode call."""
+        for sid in self._step_ids:
+            self._seq_lens[sid] += 1
+        lens = self.get_seq_lens_tensor(self._step_ids)
+        self._step_ids, self._step_bt, self._step_pos = [], None, None
+        return lens
 
     def seq_len(self, seq_id: int) -> int:
         return self._seq_lens[seq_id]

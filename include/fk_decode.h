@@ -151,6 +151,29 @@ int fk_paged_flash_decode(const void* q, const void* k_pool, const void* v_pool,
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Paged KV append: write one new token's K and V for every sequence into its
+ * page, at position positions[b] (page block_table[b, pos / 16], slot
+ * pos % 16), then add 1 to positions[b] when `increment` is non-zero.
+ * Replaces PagedKVCache.append_kv (fskernels/paged_attn/paged_kv_cache.py:109-132)
+ * driven per sequence and per layer by the paged HF adapter
+ * (benchmarks/run_hf_triton_fp8_paged.py:38-43), and the per-step
+ * quantize_to_fp8 of K/V in the FP8 adapter (triton_gqa_decode_hf_fp8.py:268-269):
+ * for an e4m3 pool the values are stored as e4m3(clamp(x / scale, +-448))
+ * with the pool's fixed per-tensor scales (device scalars).
+ *   k_new, v_new [batch, kv_heads, 128] f16/bf16  strides (s*n_b, s*n_h, 1)
+ *   k_pool, v_pool [num_pages, kv_heads, 16, 128]  pool_dtype = in_dtype or E4M3
+ *   block_table [batch, max_blocks] int32 (row stride bt_b)
+ * Pages must already be allocated; an entry outside [0, num_pages) skips the
+ * sequence and sets FK_STATUS_BAD_PAGE in *status (when non-null).
+ */
+int fk_paged_kv_append(const void* k_new, const void* v_new, int in_dtype, void* k_pool, void* v_pool,
+                       int pool_dtype, const int32_t* block_table, int32_t* positions, int increment,
+                       const float* scale_k, const float* scale_v, int* status, int batch, int kv_heads,
+                       int head_dim, int64_t num_pages, int max_blocks, int64_t skn_b, int64_t skn_h,
+                       int64_t svn_b, int64_t svn_h, int64_t sk_p, int64_t sk_h, int64_t sk_s,
+                       int64_t sv_p, int64_t sv_h, int64_t sv_s, int64_t bt_b, void* stream);
+
+/*
  * Measurement hooks (no reference counterpart: the reference times with
  * torch.profiler / triton.testing.do_bench, benchmarks/benchmark.py:87-91).
  * fk_profile_begin(n) records CUDA events on the launching stream just before

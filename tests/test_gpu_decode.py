@@ -355,3 +355,88 @@ def test_back_to_back_calls_overlapping_launches(dev):
         if i != 0:
             close(o, refs[i], **F16_TOL)
     assert N.read_status(dev) == 0
+
+
+@pytest.mark.parametrize("pool_dtype", [torch.float16, torch.bfloat16, torch.float8_e4m3fn])
+def test_paged_kv_append_matches_torch(dev, pool_dtype):
+    B, KVH, P = 5, 8, 40
+    in_dtype = torch.bfloat16 if pool_dtype == torch.bfloat16 else torch.float16
+    g = torch.Generator(device=dev).manual_seed(3)
+    k_new = torch.randn(B, KVH, 128, generator=g, device=dev).to(in_dtype)
+    v_new = torch.randn(B, KVH, 128, generator=g, device=dev).to(in_dtype)
+    kp = torch.zeros(P, KVH, 16, 128, device=dev, dtype=torch.uint8 if pool_dtype == torch.float8_e4m3fn else pool_dtype)
+    vp = torch.zeros_like(kp)
+    if pool_dtype == torch.float8_e4m3fn:
+        kp, vp = kp.view(pool_dtype), vp.view(pool_dtype)
+    bt = torch.randperm(P, generator=torch.Generator().manual_seed(1))[:B * 4].view(B, 4).to(torch.int32).to(dev)
+    pos = torch.tensor([0, 15, 16, 33, 63], dtype=torch.int32, device=dev)
+    sk = torch.tensor(0.02, device=dev)
+    sv = torch.tensor(0.03, device=dev)
+    fk.paged_attn.paged_kv_append(k_new, v_new, kp, vp, bt, pos, scale_k=sk, scale_v=sv, increment=True)
+    torch.cuda.synchronize()
+    assert pos.tolist() == [1, 16, 17, 34, 64]
+    for b, p0 in enumerate([0, 15, 16, 33, 63]):
+        phys = int(bt[b, p0 // 16])
+        if pool_dtype == torch.float8_e4m3fn:
+            ek = (k_new[b].float() / sk).clamp(-448, 448).to(pool_dtype)
+            ev = (v_new[b].float() / sv).clamp(-448, 448).to(pool_dtype)
+            assert torch.equal(kp[phys, :, p0 % 16].view(torch.uint8), ek.view(torch.uint8))
+            assert torch.equal(vp[phys, :, p0 % 16].view(torch.uint8), ev.view(torch.uint8))
+        else:
+            assert torch.equal(kp[phys, :, p0 % 16], k_new[b])
+            assert torch.equal(vp[phys, :, p0 % 16], v_new[b])
+
+
+def test_paged_cache_decode_loop_and_graph(dev):
+    # a decode loop on PagedKVCache: prompt appended, then steps of
+    # append (one kernel per layer) + decode, checked against the oracle; the
+    # last step is captured in a CUDA graph and replayed with new inputs
+    from fasterkernels_b200.paged_attn import PagedKVCache
+    L, KVH, QH = 2, 8, 32
+    cache = PagedKVCache(num_layers=L, num_pages=256, max_seqs=4, max_blocks_per_seq=64, num_kv_heads=KVH,
+                         head_dim=128, dtype=torch.float16, device=str(dev))
+    ids = [cache.allocate_sequence() for _ in range(3)]
+    g = torch.Generator(device=dev).manual_seed(9)
+    hist_k = {(l, s): [] for l in range(L) for s in ids}
+    hist_v = {(l, s): [] for l in range(L) for s in ids}
+    for step in range(40):
+        bt, pos, lens = cache.begin_step(ids)
+        for l in range(L):
+            k = torch.randn(3, KVH, 128, generator=g, device=dev).half()
+            v = torch.randn(3, KVH, 128, generator=g, device=dev).half()
+            cache.append_kv_batch(l, k, v)
+            for i, s in enumerate(ids):
+                hist_k[(l, s)].append(k[i])
+                hist_v[(l, s)].append(v[i])
+        if step % 13 == 12:
+            q = torch.randn(3, QH, 128, generator=g, device=dev).half()
+            out = fk.paged_flash_decode(q, cache.k_pool[1], cache.v_pool[1], bt, lens, 16)
+            kk = torch.cat([torch.stack(hist_k[(1, s)]) for s in ids]).float().cpu().numpy()
+            vv = torch.cat([torch.stack(hist_v[(1, s)]) for s in ids]).float().cpu().numpy()
+            cu = np.arange(0, 3 * (step + 2), step + 1)[:4]
+            close(out, O.decode_varlen(q.float().cpu().numpy(), kk, vv, cu), **F16_TOL)
+        cache.end_step()
+    # graph-captured step: append + decode on fixed buffers
+    bt, pos, lens = cache.begin_step(ids)
+    k = torch.randn(3, KVH, 128, device=dev).half()
+    v = torch.randn(3, KVH, 128, device=dev).half()
+    q = torch.randn(3, QH, 128, device=dev).half()
+    out = torch.empty_like(q)
+    fk.paged_attn.paged_kv_append(k, v, cache.k_pool[0], cache.v_pool[0], bt, pos)
+    fk.paged_flash_decode(q, cache.k_pool[0], cache.v_pool[0], bt, lens, 16, out=out)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fk.paged_attn.paged_kv_append(k, v, cache.k_pool[0], cache.v_pool[0], bt, pos)
+        fk.paged_flash_decode(q, cache.k_pool[0], cache.v_pool[0], bt, lens, 16, out=out)
+    k.copy_(torch.randn_like(k))
+    q.copy_(torch.randn_like(q))
+    graph.replay()
+    torch.cuda.synchronize()
+    for i, s in enumerate(ids):
+        hist_k[(0, s)].append(k[i])
+        hist_v[(0, s)].append(v[i])
+    kk = torch.cat([torch.stack(hist_k[(0, s)]) for s in ids]).float().cpu().numpy()
+    vv = torch.cat([torch.stack(hist_v[(0, s)]) for s in ids]).float().cpu().numpy()
+    n = len(hist_k[(0, ids[0])])
+    close(out, O.decode_varlen(q.float().cpu().numpy(), kk, vv, np.arange(0, 3 * n + 1, n)), **F16_TOL)

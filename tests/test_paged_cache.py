@@ -82,3 +82,20 @@ def test_lpt_partition_balances():
         assert sorted(i for p in parts for i in p) == list(range(len(lens)))
         loads = [sum(lens[i] for i in p) for p in parts]
         assert max(loads) / (sum(lens) / n) < 1.002
+
+
+def test_begin_end_step_host_bookkeeping():
+    c = make(pages=8, seqs=3, blocks=4)
+    a, b = c.allocate_sequence(), c.allocate_sequence()
+    z = torch.zeros(1, 2, 1, 128, dtype=torch.float16)
+    for _ in range(15):
+        c.append_kv(a, 0, z, z)
+    bt, pos, lens = c.begin_step([a, b])
+    # a (15 tokens) still fits its first page; b (0 tokens) gets a new page
+    assert pos.tolist() == [15, 0] and lens.tolist() == [16, 1]
+    assert c.pages_used == 2 and int(c.block_table[b, 0]) >= 0
+    assert bt.shape == (2, 4) and bt[0, 0] == c.block_table[a, 0]
+    new_lens = c.end_step()
+    assert new_lens.tolist() == [16, 1] and c.seq_len(a) == 16
+    c.begin_step([a])  # a crosses into its second page
+    assert c.pages_used == 3 and int(c.block_table[a, 1]) >= 0
