@@ -118,29 +118,85 @@ def _module_sinks(module, q_heads, dev):
     return sinks.detach().to(device=dev, dtype=torch.float32).reshape(-1)
 
 
-def _decode_window(kwargs, bsz, dev):
-    """cache_lens (and the sliding-window start) from ``cache_position``, with
-    tensor ops only (graph-safe), as triton_gqa_decode_hf.py:239-250 does.
-    The window is [max(0, len - window), len)."""
+def _decode_window(kwargs, bsz, dev, attention_mask=None, cache_len=None):
+    """(cache_lens, start offsets or None) for a q_len == 1 call, with tensor
+    ops only (graph-safe).
+    * ``cache_position`` given (the reference's runner passes it,
+      fskernels/engine/cuda_graph_runner.py:193,211): length = position + 1,
+      as triton_gqa_decode_hf.py:239-242 computes it; a ``sliding_window``
+      gives the window [max(0, len - window), len).
+    * otherwise (transformers 5.x no longer passes ``cache_position``): the
+      attended range of each row is the span of its valid mask positions
+      (left padding becomes a start offset), or the whole cache without a mask.
+    """
     cache_position = kwargs.get("cache_position")
-    lens = (cache_position[-1:] + 1).to(torch.int32).expand(bsz).contiguous()
-    window = kwargs.get("sliding_window")
     starts = None
+    if cache_position is not None:
+        lens = (cache_position[-1:] + 1).to(torch.int32).expand(bsz).contiguous()
+    elif attention_mask is not None:
+        m = attention_mask.reshape(attention_mask.shape[0], -1)[:, -int(cache_len):]
+        valid = m if m.dtype == torch.bool else (m == 0)
+        valid = valid.expand(bsz, -1)
+        S = valid.shape[1]
+        first = torch.argmax(valid.to(torch.int32), dim=1)
+        last = S - torch.argmax(valid.flip(1).to(torch.int32), dim=1)
+        any_valid = valid.any(dim=1)
+        lens = torch.where(any_valid, last, torch.zeros_like(last)).to(torch.int32).contiguous()
+        starts = torch.where(any_valid, first, torch.zeros_like(first)).to(torch.int32).contiguous()
+    else:
+        lens = torch.full((bsz,), int(cache_len), dtype=torch.int32, device=dev)
+    window = kwargs.get("sliding_window")
     if window is not None:
-        starts = torch.clamp(lens - int(window), min=0).to(torch.int32)
+        wstart = torch.clamp(lens - int(window), min=0).to(torch.int32)
+        starts = wstart if starts is None else torch.maximum(starts, wstart)
     return lens, starts
+
+
+def _fallback(module, query_states, key_states, value_states, attention_mask, scaling, dropout, **kwargs):
+    """Prefill / non-decode calls: transformers' own SDPA attention (the
+    reference falls back to the native eager attention the same way,
+    triton_gqa_decode_hf.py:256-258)."""
+    try:
+        from transformers.integrations.sdpa_attention import sdpa_attention_forward
+        return sdpa_attention_forward(module, query_states, key_states, value_states, attention_mask,
+                                      scaling=scaling, dropout=dropout, **kwargs)
+    except ImportError:  # pragma: no cover
+        from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
+        return eager_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling,
+                                       dropout, **kwargs)
+
+
+def _is_decode(kwargs, query_states):
+    return (query_states.shape[2] == 1 and query_states.is_cuda and query_states.shape[-1] == HEAD_DIM
+            and (kwargs.get("past_key_values") is not None or kwargs.get("cache_position") is not None))
 
 
 def custom_hf_decode_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling: float,
                                        dropout: float = 0.0, **kwargs) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """HF attention-interface function: a decode step (q_len == 1 with a KV
+    cache) runs the sm_100a kernel and returns ([B, Q_H, D], None), which the
+    model reshapes to [B, 1, Q_H * D] as it does the reference's output
+    (triton_gqa_decode_hf.py:218-258); anything else goes to transformers' SDPA."""
     bsz, q_heads, q_len, head_dim = query_states.shape
-    if (kwargs.get("past_key_values") is not None and q_len == 1 and kwargs.get("cache_position") is not None
-            and query_states.is_cuda and head_dim == HEAD_DIM):
+    if _is_decode(kwargs, query_states):
         q = query_states.squeeze(2)
-        lens, starts = _decode_window(kwargs, bsz, q.device)
+        lens, starts = _decode_window(kwargs, bsz, q.device, attention_mask, key_states.shape[2])
         out = dense_decode(q, key_states, value_states, lens, starts,
                            s_aux=_module_sinks(module, q_heads, q.device))
         return out, None
-    from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
-    return eager_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling, dropout,
-                                   **kwargs)
+    return _fallback(module, query_states, key_states, value_states, attention_mask, scaling, dropout, **kwargs)
+
+
+def register_attention_interface(name: str = "fk_decode", fp8: bool = False) -> str:
+    """Register the adapter with transformers' ``AttentionInterface`` so that
+    ``attn_implementation=name`` selects it for any model (the reference's
+    module-global patch of ``eager_attention_forward``,
+    fskernels/engine/fs_inference_engine.py:12-13, only takes effect under
+    "eager" in transformers 5.x).  Returns the registered name."""
+    from transformers import AttentionInterface
+    if fp8:
+        from .gqa_decode_hf_fp8 import custom_hf_decode_attention_forward_fp8 as fn
+    else:
+        fn = custom_hf_decode_attention_forward
+    AttentionInterface.register(name, fn)
+    return name

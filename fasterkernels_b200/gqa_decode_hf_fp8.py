@@ -20,7 +20,7 @@ from typing import Optional, Tuple
 import torch
 
 from .gqa_decode import HEAD_DIM
-from .gqa_decode_hf import _decode_window, _module_sinks, dense_decode
+from .gqa_decode_hf import _decode_window, _fallback, _is_decode, _module_sinks, dense_decode
 
 FP8_DTYPE = torch.float8_e4m3fn
 FP8_MAX = 448.0
@@ -67,11 +67,10 @@ def custom_hf_decode_attention_forward_fp8(module, query_states, key_states, val
     per-tensor scales, then decode.  A cache that is already e4m3 (with
     ``module.k_scale``/``module.v_scale`` tensors) is used without re-quantising."""
     bsz, q_heads, q_len, head_dim = query_states.shape
-    if (kwargs.get("past_key_values") is not None and q_len == 1 and kwargs.get("cache_position") is not None
-            and query_states.is_cuda and head_dim == HEAD_DIM):
+    if _is_decode(kwargs, query_states):
         out_dtype = query_states.dtype
         q = query_states.squeeze(2)
-        lens, starts = _decode_window(kwargs, bsz, q.device)
+        lens, starts = _decode_window(kwargs, bsz, q.device, attention_mask, key_states.shape[2])
         q8, sq = quantize_to_fp8(q)
         if key_states.dtype == FP8_DTYPE:
             k8, sk = key_states, getattr(module, "k_scale")
@@ -82,6 +81,4 @@ def custom_hf_decode_attention_forward_fp8(module, query_states, key_states, val
         out = flash_decode_gqa_hf_fp8(q8, k8, v8, lens, sq, sk, sv, out_dtype, start_k_offsets=starts,
                                       s_aux=_module_sinks(module, q_heads, q.device))
         return out, None
-    from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
-    return eager_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling, dropout,
-                                   **kwargs)
+    return _fallback(module, query_states, key_states, value_states, attention_mask, scaling, dropout, **kwargs)

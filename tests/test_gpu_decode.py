@@ -440,3 +440,21 @@ def test_paged_cache_decode_loop_and_graph(dev):
     vv = torch.cat([torch.stack(hist_v[(0, s)]) for s in ids]).float().cpu().numpy()
     n = len(hist_k[(0, ids[0])])
     close(out, O.decode_varlen(q.float().cpu().numpy(), kk, vv, np.arange(0, 3 * n + 1, n)), **F16_TOL)
+
+
+def test_hf_adapter_mask_derived_window(dev):
+    # transformers 5.x style call: no cache_position, a padding mask
+    class M:
+        num_key_value_heads = 8
+    B, S = 3, 700
+    qs = torch.randn(B, 32, 1, 128, device=dev, dtype=torch.float16)
+    ks = torch.randn(B, 8, S, 128, device=dev, dtype=torch.float16)
+    vs = torch.randn(B, 8, S, 128, device=dev, dtype=torch.float16)
+    mask = torch.ones(B, 1, 1, S, dtype=torch.bool, device=dev)
+    mask[0, ..., :100] = False   # left padding
+    mask[2, ..., :650] = False
+    out, _ = fk.custom_hf_decode_attention_forward(M(), qs, ks, vs, mask, 128 ** -0.5, past_key_values=object())
+    ref = O.decode_dense(qs.squeeze(2).float().cpu().numpy(), ks.float().cpu().numpy(), vs.float().cpu().numpy(),
+                         [S, S, S], [100, 0, 650])
+    close(out, ref, **F16_TOL)
+    fk.register_attention_interface("fk_decode_gpu_test")
