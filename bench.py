@@ -52,50 +52,58 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled during the timed region: NVML
+    polled from a thread every ~2 ms (read-only queries), with nvidia-smi as
+    the fallback.  The timed region of a decode bench is tens of ms, so a
+    100 ms nvidia-smi period would catch almost nothing."""
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
-        self.rows = []
-        self.proc = None
+        self.sm, self.mask = [], 0
+        self.max_mhz = None
+        self.th = None
+        self.stop_flag = False
+        self.err = None
+
+    def _poll(self, nv, h):
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag:
+            try:
+                self.sm.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                self.mask |= int(get_reasons(h))
+            except Exception as e:  # pragma: no cover
+                self.err = repr(e)
+                return
+            time.sleep(0.002)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.th = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[self.idx]) if vis and vis.split(",")[self.idx].isdigit() else self.idx
+            h = nv.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.nv = nv
+            self.th = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
             self.th.start()
-        except Exception:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+        except Exception as e:
+            self.err = repr(e)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in self.rows:
-            if len(r) >= 9:
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        self.stop_flag = True
+        if self.th is not None:
+            self.th.join(timeout=2)
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [f"no samples ({self.err})"]}
+        reasons = sorted(n for n, attr in self.REASONS.items() if self.mask & int(getattr(self.nv, attr, 0)))
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.sm), "source": "NVML, 2 ms"}
 
 
 # ---------------------------------------------------------------- workloads

@@ -44,11 +44,12 @@ def lib() -> ctypes.CDLL:
     with _lib_lock:
         if _lib is not None:
             return _lib
-        if not os.path.exists(LIB_PATH):
+        path = os.environ.get("FK_DECODE_LIB", LIB_PATH)  # alternate build, e.g. for A/B timing
+        if not os.path.exists(path):
             raise RuntimeError(
-                f"fasterkernels_b200 native library not found at {LIB_PATH}; build it with "
+                f"fasterkernels_b200 native library not found at {path}; build it with "
                 "`python -m fasterkernels_b200.build` (needs nvcc with sm_100a support)")
-        L = ctypes.CDLL(LIB_PATH)
+        L = ctypes.CDLL(path)
         L.fk_version.restype = _I
         L.fk_version.argtypes = []
         L.fk_last_error.restype = ctypes.c_char_p
