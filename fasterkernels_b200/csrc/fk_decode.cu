@@ -941,6 +941,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     g_trace[blockIdx.x][2] = gtimer();
     g_trace[blockIdx.x][3] = tr_nseg;
     g_trace[blockIdx.x][4] = tr_ntile;
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_trace[blockIdx.x][9] = smid;
   }
 #endif
 }
