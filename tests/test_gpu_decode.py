@@ -458,3 +458,63 @@ def test_hf_adapter_mask_derived_window(dev):
                          [S, S, S], [100, 0, 650])
     close(out, ref, **F16_TOL)
     fk.register_attention_interface("fk_decode_gpu_test")
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+def test_fp8_paged_group_sizes(dev, G):
+    lens = [1, 31, 32, 33, 1500, 0, 4097]
+    d = W.make_varlen(lens, 4 * G, 4, torch.float32, dev, seed=50 + G, sinks=True)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    q = d["q"].half()
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=G)
+    out = fk.paged_flash_decode(q, kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn), bt,
+                                torch.tensor(lens, dtype=torch.int32, device=dev), 16, s_aux=d["s_aux"],
+                                scale_k=sk, scale_v=sv)
+    ref = O.decode_varlen(q.float().cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
+                          d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
+    close(out, ref, atol=3e-3, rtol=1e-2)
+
+
+def test_fp8_dense_bf16_query_and_output(dev):
+    B, S = 3, 3000
+    lens = [2999, 1, 1800]
+    g = torch.Generator(device=dev).manual_seed(60)
+    q = torch.randn(B, 32, 128, generator=g, device=dev).bfloat16()
+    k = torch.randn(B, 8, S, 128, generator=g, device=dev)
+    v = torch.randn(B, 8, S, 128, generator=g, device=dev)
+    k8, sk = W.quantize_e4m3(k)
+    v8, sv = W.quantize_e4m3(v)
+    out = fk.flash_decode_gqa_hf_fp8(q, k8, v8, torch.tensor(lens, dtype=torch.int32, device=dev), None, sk, sv,
+                                     torch.bfloat16)
+    assert out.dtype == torch.bfloat16
+    ref = O.decode_dense(q.float().cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
+                         lens)
+    close(out, ref, **BF16_TOL)
+
+
+def test_dense_strided_cache_views(dev):
+    # caches that are slices of larger allocations (HF StaticCache style) and
+    # a query with a non-trivial batch stride
+    big_k = torch.randn(4, 8, 5000, 128, device=dev, dtype=torch.float16)
+    big_v = torch.randn(4, 8, 5000, 128, device=dev, dtype=torch.float16)
+    kc, vc = big_k[1:3, :, :4096], big_v[1:3, :, :4096]
+    qbig = torch.randn(2, 48, 128, device=dev, dtype=torch.float16)
+    q = qbig[:, 8:40]
+    lens = torch.tensor([4096, 2500], dtype=torch.int32, device=dev)
+    starts = torch.tensor([0, 1000], dtype=torch.int32, device=dev)
+    out = fk.flash_decode_gqa_hf_dense_optimized(q, kc, vc, lens, starts)
+    ref = O.decode_dense(q.float().cpu().numpy(), kc.float().cpu().numpy(), vc.float().cpu().numpy(), [4096, 2500],
+                         [0, 1000])
+    close(out, ref, **F16_TOL)
+
+
+def test_paged_strided_block_table(dev):
+    lens = [100, 2000, 700]
+    q, k, v, cu, s = _rand_case(dev, lens, 32, 8, torch.float16, True, seed=61)
+    kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.5, seed=61)
+    wide = torch.full((3, 2 * bt.shape[1] + 5), -1, dtype=torch.int32, device=dev)
+    wide[:, : bt.shape[1]] = bt
+    out = fk.paged_flash_decode(q, kp, vp, wide[:, : bt.shape[1] + 3], torch.tensor(lens, dtype=torch.int32,
+                                                                                     device=dev), 16, s_aux=s)
+    assert torch.equal(out, fk.flash_decode_gqa_varlen(q, k, v, cu, s))
