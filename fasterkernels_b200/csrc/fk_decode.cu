@@ -322,6 +322,31 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     }
     fence_mbar_init();
   }
+  // Plan, with every thread of the CTA: thread t sums the granules of
+  // sequences [t*bpt, (t+1)*bpt) (independent loads, one round trip); warp 0
+  // turns the per-thread sums into exclusive prefixes.
+  __shared__ long long s_psum[THREADS];
+  __shared__ long long s_pexc[THREADS];
+  const int bpt = (p.B + THREADS - 1) / THREADS;
+  {
+    long long mysum = 0;
+    const int b0 = threadIdx.x * bpt, b1 = min(b0 + bpt, p.B);
+    for (int b = b0; b < b1; ++b) {
+      long long t0;
+      mysum += (seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE;
+    }
+    s_psum[threadIdx.x] = mysum;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    long long run = 0;
+    for (int base = 0; base < THREADS; base += 32) {
+      const long long v = s_psum[base + lane];
+      const long long inc = warp_incl_scan(v, lane);
+      s_pexc[base + lane] = run + inc - v;
+      run += __shfl_sync(0xffffffffu, inc, 31);
+    }
+  }
   __syncthreads();
   // Let the next decode kernel in the stream start its CTAs (planning and
   // KV loads) as SMs free up; its epilogue warps wait for this grid.
@@ -335,16 +360,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     }
     const long long NI = KVI;
     const float psq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
-    // Plan: total granules of the whole batch.
-    long long tot = 0;
-    for (int base = 0; base < p.B; base += 32) {
-      const int b = base + lane;
-      long long t0;
-      long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-      tot += n;
-    }
+    const long long tot = s_pexc[THREADS - 1] + s_psum[THREADS - 1];  // granules of the whole batch
     const long long U = tot * NI;
     const long long S = p.num_ctas;
     const long long per = max((U + S - 1) / S, static_cast<long long>(MIN_PER));
@@ -375,23 +391,47 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       }
     };
 
+    // Q words of the next item, prefetched into registers: lane owns words
+    // lane + 32k of the [HP][8 heads][64 pairs] block; paged: a window of 32
+    // block-table entries (one per lane) + the next one.
+    constexpr int QW = HP * GPAD * 64 / 32;
+    uint32_t qpre[QW];
+    int qpre_b = -1, qpre_h = -1;
+    auto q_prefetch = [&](int bb, int ih) {
+      const long long qb0 = static_cast<long long>(bb) * p.q_sb;
+#pragma unroll
+      for (int k = 0; k < QW; ++k) {
+        const int idx = lane + 32 * k;
+        const int hh = idx / (GPAD * 64), j = (idx >> 6) & (GPAD - 1), d = (idx & 63) * 2;
+        const int qh = (ih * HP + hh) * p.G + j;
+        qpre[k] = (j < p.G) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d) : 0u;
+      }
+      qpre_b = bb;
+      qpre_h = ih;
+    };
+    int win_b = -1;
+    int win_p0 = 0;
+    int bt_cur = -1, bt_nxt = -1;
+    auto ld_bt = [&](int bb, int pg) -> int {
+      return (pg < p.max_blocks) ? __ldg(p.bt + static_cast<long long>(bb) * p.bt_sb + pg) : -1;
+    };
+
     if (start < end) {
-      // Locate the first item of this CTA's granule range.
-      int bs = -1;
-      long long preb = 0, run = 0;
-      for (int base = 0; base < p.B && bs < 0; base += 32) {
-        const int b = base + lane;
+      // Locate the first item of this CTA's granule range: the thread block
+      // of sequences containing `start`, then the sequence inside it.
+      int kt = -1;
+      for (int base = 0; base < THREADS && kt < 0; base += 32) {
+        const long long e = s_pexc[base + lane], n = s_psum[base + lane];
+        const unsigned m = __ballot_sync(0xffffffffu, n > 0 && NI * (e + n) > start);
+        if (m) kt = base + __ffs(m) - 1;
+      }
+      int bs = kt * bpt;
+      long long preb = s_pexc[kt];
+      for (;; ++bs) {
         long long t0;
-        const long long n = (b < p.B) ? ((seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE) : 0;
-        const long long inc = warp_incl_scan(n, lane);
-        const bool hit = (b < p.B) && (NI * (run + inc) > start);
-        const unsigned m = __ballot_sync(0xffffffffu, hit);
-        if (m) {
-          const int L = __ffs(m) - 1;
-          bs = base + L;
-          preb = run + __shfl_sync(0xffffffffu, inc - n, L);
-        }
-        run += __shfl_sync(0xffffffffu, inc, 31);
+        const long long n = (seq_len<LAYOUT>(p, bs, &t0) + PAGE - 1) / PAGE;
+        if (NI * (preb + n) > start) break;
+        preb += n;
       }
       int b = bs;
       long long tok0;
@@ -401,34 +441,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       long long item_base = NI * preb + static_cast<long long>(hi) * nb;
       long long pos = start;
 
-      // Q words of the next item, prefetched into registers: lane owns words
-      // lane + 32k of the [HP][8 heads][64 pairs] block.
-      constexpr int QW = HP * GPAD * 64 / 32;
-      uint32_t qpre[QW];
-      int qpre_b = -1, qpre_h = -1;
-      auto q_prefetch = [&](int bb, int ih) {
-        const long long qb0 = static_cast<long long>(bb) * p.q_sb;
-#pragma unroll
-        for (int k = 0; k < QW; ++k) {
-          const int idx = lane + 32 * k;
-          const int hh = idx / (GPAD * 64), j = (idx >> 6) & (GPAD - 1), d = (idx & 63) * 2;
-          const int qh = (ih * HP + hh) * p.G + j;
-          qpre[k] = (j < p.G) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d) : 0u;
-        }
-        qpre_b = bb;
-        qpre_h = ih;
-      };
       // length of the next sequence, prefetched
       long long ntok0 = 0;
       int nlen = (b + 1 < p.B) ? seq_len<LAYOUT>(p, b + 1, &ntok0) : 0;
-
-      // PAGED: window of 32 block-table entries (one per lane) + the next one.
-      int win_b = -1;
-      int win_p0 = 0;
-      int bt_cur = -1, bt_nxt = -1;
-      auto ld_bt = [&](int bb, int pg) -> int {
-        return (pg < p.max_blocks) ? __ldg(p.bt + static_cast<long long>(bb) * p.bt_sb + pg) : -1;
-      };
 
       while (alive && pos < end) {
         const long long seg_hi = min(end, item_base + nb);
@@ -695,6 +710,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       }
       if (et == 0) cnt[item] = 0;
     }
+#ifdef FK_TRACE
+    if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][9] = gtimer();
+#endif
     return;
   }
 
@@ -941,9 +959,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     g_trace[blockIdx.x][2] = gtimer();
     g_trace[blockIdx.x][3] = tr_nseg;
     g_trace[blockIdx.x][4] = tr_ntile;
-    unsigned smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    g_trace[blockIdx.x][9] = smid;
+
   }
 #endif
 }
