@@ -261,9 +261,10 @@ __device__ __forceinline__ float finalize(float A, float L, float M, const float
 
 #ifdef FK_TRACE
 // Per-CTA timeline for performance investigation builds (-DFK_TRACE):
-// [start, first tile, end (ns), segments, tiles, producer switch ns, producer acquire-wait ns,
-//  consumer wait ns at first tiles of segments, consumer wait ns at other tiles, 0]
-__device__ unsigned long long g_trace[4096][10];
+// [start, first tile, consumer end (ns), segments, tiles, producer switch ns, producer acquire-wait ns,
+//  consumer wait ns at first tiles of segments, consumer wait ns at other tiles, epilogue end (ns),
+//  SM id, producer cycles in block-table lookup, in Q staging, in issue, per whole tile]
+__device__ unsigned long long g_trace[4096][16];
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -305,8 +306,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 
 #ifdef FK_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 4096) {
-    for (int i = 1; i < 10; ++i) g_trace[blockIdx.x][i] = 0;
+    for (int i = 1; i < 16; ++i) g_trace[blockIdx.x][i] = 0;
     g_trace[blockIdx.x][0] = gtimer();
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_trace[blockIdx.x][10] = smid;
   }
   unsigned long long tr_nseg = 0, tr_ntile = 0;
   bool tr_first = true;
@@ -409,6 +413,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       qpre_b = bb;
       qpre_h = ih;
     };
+#ifdef FK_TRACE
+    long long tr_c[4] = {0, 0, 0, 0};  // producer cycles: block table, Q staging, issue, whole tile
+#endif
     int win_b = -1;
     int win_p0 = 0;
     int bt_cur = -1, bt_nxt = -1;
@@ -461,10 +468,16 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 #endif
         for (int tt = tbeg; tt < tend; tt += TT) {
           const int valid = min(TT, tend - tt);
+#ifdef FK_TRACE
+          const long long tc0 = clock64();
+#endif
           if (!acquire()) {
             alive = false;
             break;
           }
+#ifdef FK_TRACE
+          const long long tc1 = clock64();
+#endif
           const uint32_t sK = smem_u32(stages + stage * C::STAGE_BYTES);
           const uint32_t sV = sK + C::TILE_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
@@ -493,6 +506,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
             if (lane == 0 && bad) atomicOr(&hdr->status, FK_STATUS_BAD_PAGE);
             if (!okp) phys = -1;
           }
+#ifdef FK_TRACE
+          const long long tc2 = clock64();
+#endif
           if (tt == tbeg) {
             // Q rows of the item -> qstage[stage] as packed MMA-type pairs,
             // from the registers prefetched one item ahead
@@ -506,6 +522,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
             __threadfence_block();
             __syncwarp();
           }
+#ifdef FK_TRACE
+          const long long tc3 = clock64();
+#endif
           if (lane == 0) {
             Meta& mt = meta[stage];
             mt.b = b;
@@ -555,6 +574,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           }
 #ifdef FK_TRACE
           if (tt == tbeg && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][5] += gtimer() - tr_sw0;
+          {
+            const long long tc4 = clock64();
+            tr_c[0] += tc2 - tc1;
+            tr_c[1] += tc3 - tc2;
+            tr_c[2] += tc4 - tc3;
+            tr_c[3] += tc4 - tc0;
+          }
 #endif
           advance();
         }
@@ -574,6 +600,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         item_base = NI * preb + static_cast<long long>(hi) * nb;
       }
     }
+#ifdef FK_TRACE
+    if (lane == 0 && blockIdx.x < 4096)
+      for (int i = 0; i < 4; ++i) g_trace[blockIdx.x][11 + i] = tr_c[i];
+#endif
     // End-of-work marker.
     if (alive && acquire()) {
       if (lane == 0) {
@@ -1527,6 +1557,6 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
 
 #ifdef FK_TRACE
 extern "C" int fk_trace_read(unsigned long long* host, int n) {
-  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 10 * n) == cudaSuccess ? 0 : 1;
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 16 * n) == cudaSuccess ? 0 : 1;
 }
 #endif

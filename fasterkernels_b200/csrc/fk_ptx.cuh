@@ -45,18 +45,29 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase of parity `parity` to complete.  Polls, then
-// backs off with nanosleep; gives up after roughly four seconds and returns
-// false so that the caller can record FK_STATUS_TIMEOUT and leave the loop
-// instead of hanging the GPU.
+// Bounded wait for the phase of parity `parity` to complete.  try_wait
+// suspends the thread in hardware until the phase completes or a short
+// system-defined limit passes, so the loop wakes as soon as the phase flips;
+// it gives up after about four seconds of %globaltimer and returns false so
+// that the caller can record FK_STATUS_TIMEOUT and leave its loop instead of
+// hanging the GPU.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
 #pragma unroll 1
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
+  while (true) {
+#ifdef FK_WAIT_SLEEP
+    __nanosleep(FK_WAIT_SLEEP);
+#endif
     if (mbar_test(bar, parity)) return true;
-    if (it > 64) __nanosleep(1000);
+    if (global_ns() - t0 > 4000000000ull) return false;
   }
-  return false;
 }
 
 // ------------------------------------------------------------------- TMA
