@@ -181,6 +181,7 @@ struct Params {
   int B, q_heads, kv_heads, G;
   int q_dtype, out_dtype;
   int num_ctas;
+  int q_al16;  // q base and strides 16-byte aligned (rows can be copied with cp.async)
 };
 
 // Effective length of sequence b and the coordinate of its first token.
@@ -246,17 +247,24 @@ __device__ __forceinline__ void store_out(const Params& p, long long idx, float 
     static_cast<__half*>(p.out)[idx] = __float2half_rn(v);
 }
 
-// Normalisation of one (query head, dim) output with the oracle's sink
-// formula.  A, L are relative to the running max M (log2 domain).
-__device__ __forceinline__ float finalize(float A, float L, float M, const float* s_aux, int qh, float sv) {
+// Normalisation of query head qh with the oracle's sink formula.  L and the
+// head's accumulators A are relative to its running max M (log2 domain):
+// out = (A * e) / Lf * scale_v with e = 2^(M - Ms), Lf = L e + 2^(s - Ms),
+// Ms = max(M, s); without a sink e = 1 and Lf = L.
+__device__ __forceinline__ void sink_norm(float L, float M, const float* s_aux, int qh, float* e, float* Lf) {
   if (s_aux != nullptr) {
     const float s2 = __ldg(s_aux + qh) * LOG2E;
     const float Ms = fmaxf(M, s2);
-    const float e = exp2f(M - Ms);
-    A *= e;
-    L = L * e + exp2f(s2 - Ms);
+    *e = exp2f(M - Ms);
+    *Lf = L * *e + exp2f(s2 - Ms);
+  } else {
+    *e = 1.f;
+    *Lf = L;
   }
-  return L > 0.f ? (A / L) * sv : 0.f;
+}
+
+__device__ __forceinline__ float norm_out(float A, float e, float Lf, float sv) {
+  return Lf > 0.f ? ((A * e) / Lf) * sv : 0.f;
 }
 
 #ifdef FK_TRACE
@@ -264,7 +272,7 @@ __device__ __forceinline__ float finalize(float A, float L, float M, const float
 // [start, first tile, consumer end (ns), segments, tiles, producer switch ns, producer acquire-wait ns,
 //  consumer wait ns at first tiles of segments, consumer wait ns at other tiles, epilogue end (ns),
 //  SM id, producer cycles in block-table lookup, in Q staging, in issue, per whole tile]
-__device__ unsigned long long g_trace[4096][16];
+__device__ unsigned long long g_trace[4096][24];
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -306,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 
 #ifdef FK_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 4096) {
-    for (int i = 1; i < 16; ++i) g_trace[blockIdx.x][i] = 0;
+    for (int i = 1; i < 24; ++i) g_trace[blockIdx.x][i] = 0;
     g_trace[blockIdx.x][0] = gtimer();
     unsigned smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
@@ -325,6 +333,19 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       mbar_init(smem_u32(&eempty[s]), ETHREADS);
     }
     fence_mbar_init();
+  }
+  // Q already of the MMA type and 16-byte aligned: each segment's Q rows are
+  // copied straight into the stage's Q slot by cp.async, completing on the
+  // stage's full barrier with the KV tiles; the padding rows (heads G..7) are
+  // zeroed once, here.  Otherwise the producer converts Q through registers.
+  const bool q_async = p.q_al16 && p.q_dtype == (C::BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16);
+  if (q_async && p.G < GPAD) {
+    const int npad = GPAD - p.G;
+    for (int u = threadIdx.x; u < C::STAGES * HP * npad * 16; u += THREADS) {
+      const int row = u >> 4, c = u & 15;  // row over (stage, head, padding head)
+      const int sh = row / npad, j = p.G + row % npad;
+      reinterpret_cast<uint4*>(qstage + sh * (GPAD * 64) + j * 64)[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
   // Plan, with every thread of the CTA: thread t sums the granules of
   // sequences [t*bpt, (t+1)*bpt) (independent loads, one round trip); warp 0
@@ -352,6 +373,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     }
   }
   __syncthreads();
+#ifdef FK_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][16] = gtimer();
+#endif
   // Let the next decode kernel in the stream start its CTAs (planning and
   // KV loads) as SMs free up; its epilogue warps wait for this grid.
   grid_dependency_trigger();
@@ -364,6 +388,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
     }
     const long long NI = KVI;
     const float psq = (p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
+
     const long long tot = s_pexc[THREADS - 1] + s_psum[THREADS - 1];  // granules of the whole batch
     const long long U = tot * NI;
     const long long S = p.num_ctas;
@@ -451,6 +476,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       // length of the next sequence, prefetched
       long long ntok0 = 0;
       int nlen = (b + 1 < p.B) ? seq_len<LAYOUT>(p, b + 1, &ntok0) : 0;
+#ifdef FK_TRACE
+      if (lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][17] = gtimer() + 0 * nlen;
+      bool tr_f = true;
+#endif
 
       while (alive && pos < end) {
         const long long seg_hi = min(end, item_base + nb);
@@ -508,22 +537,37 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           }
 #ifdef FK_TRACE
           const long long tc2 = clock64();
+          if (tr_f && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][18] = gtimer();
 #endif
           if (tt == tbeg) {
-            // Q rows of the item -> qstage[stage] as packed MMA-type pairs,
-            // from the registers prefetched one item ahead
-            if (qpre_b != b || qpre_h != hi) q_prefetch(b, hi);
             uint32_t* qs = qstage + stage * QWORDS;
+            if (q_async) {
+              // the item's HP*G rows of 256 bytes, 16 bytes per copy
+              const uint32_t qd = smem_u32(qs);
+              const long long qb0 = static_cast<long long>(b) * p.q_sb;
+              for (int u = lane; u < HP * p.G * 16; u += 32) {
+                const int hh = u / (p.G * 16), j = (u >> 4) % p.G, c = u & 15;
+                const int qh = (hi * HP + hh) * p.G + j;
+                cp_async16(qd + (hh * GPAD + j) * 256 + c * 16,
+                           static_cast<const unsigned short*>(p.q) + qb0 + static_cast<long long>(qh) * p.q_sh + c * 8);
+              }
+              cp_async_mbar_arrive(fb);
+            } else {
+              // Q rows of the item -> qstage[stage] as packed MMA-type pairs,
+              // from the registers prefetched one item ahead
+              if (qpre_b != b || qpre_h != hi) q_prefetch(b, hi);
 #pragma unroll
-            for (int k = 0; k < QW; ++k) qs[lane + 32 * k] = q_pair_to_mma<C::BF16>(p, qpre[k], psq);
-            // start fetching the next item's Q
-            if (hi + 1 < KVI) q_prefetch(b, hi + 1);
-            else if (b + 1 < p.B) q_prefetch(b + 1, 0);
-            __threadfence_block();
+              for (int k = 0; k < QW; ++k) qs[lane + 32 * k] = q_pair_to_mma<C::BF16>(p, qpre[k], psq);
+              // start fetching the next item's Q
+              if (hi + 1 < KVI) q_prefetch(b, hi + 1);
+              else if (b + 1 < p.B) q_prefetch(b + 1, 0);
+              __threadfence_block();
+            }
             __syncwarp();
           }
 #ifdef FK_TRACE
           const long long tc3 = clock64();
+          if (tr_f && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][19] = gtimer();
 #endif
           if (lane == 0) {
             Meta& mt = meta[stage];
@@ -574,6 +618,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           }
 #ifdef FK_TRACE
           if (tt == tbeg && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][5] += gtimer() - tr_sw0;
+          if (tr_f && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][20] = gtimer();
+          tr_f = false;
           {
             const long long tc4 = clock64();
             tr_c[0] += tc2 - tc1;
@@ -635,50 +681,79 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       }
     }
     const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
-    constexpr int DPT = HEAD_DIM / ETHREADS;           // dims per epilogue thread
     int eb = 0;
     uint32_t eph = 0;
     while (true) {
+#ifdef FK_TRACE
+      const unsigned long long te0 = gtimer();
+#endif
       if (!mbar_wait(smem_u32(&efull[eb]), eph)) {
         if (et == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
         break;
       }
+#ifdef FK_TRACE
+      const unsigned long long te1 = gtimer();
+      if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][23] += te1 - te0;
+#endif
       const Meta mt = emeta[eb];
       if (mt.flags & F_END) break;
       const EpiSlot& E = eslot[eb];
       const bool whole = (mt.flags & F_WHOLE) != 0;
       const long long item = static_cast<long long>(mt.b) * KVI + mt.h;
       const long long obase = static_cast<long long>(mt.b) * p.o_sb;
+      // One unit per thread and round: query head hd of KV head hh (head
+      // slot u / 8), dims (u % 8) * 4 + 32 k, k < 4 (a quarter warp reads
+      // 128 contiguous bytes of the slot: no bank conflicts).
+      for (int u = et; u < HP * p.G * 8; u += ETHREADS) {
+        const int hh = u / (p.G * 8), hd = (u >> 3) % p.G, d4 = (u & 7) * 4;
+        float M = NEG_INF;
 #pragma unroll
-      for (int hh = 0; hh < HP; ++hh) {
-        for (int hd = 0; hd < p.G; ++hd) {
-          float M = NEG_INF;
+        for (int w = 0; w < WPH; ++w) M = fmaxf(M, E.cm[hh * WPH + w][hd]);
+        float ew[WPH], L = 0.f;
 #pragma unroll
-          for (int w = 0; w < WPH; ++w) M = fmaxf(M, E.cm[hh * WPH + w][hd]);
-          float ew[WPH], L = 0.f;
+        for (int w = 0; w < WPH; ++w) {
+          ew[w] = (M == NEG_INF) ? 0.f : exp2f(E.cm[hh * WPH + w][hd] - M);
+          L += ew[w] * E.cl[hh * WPH + w][hd];
+        }
+        float4 A[4];
 #pragma unroll
-          for (int w = 0; w < WPH; ++w) {
-            ew[w] = (M == NEG_INF) ? 0.f : exp2f(E.cm[hh * WPH + w][hd] - M);
-            L += ew[w] * E.cl[hh * WPH + w][hd];
+        for (int k = 0; k < 4; ++k) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < WPH; ++w) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float4 v = *reinterpret_cast<const float4*>(&E.cacc[hh * WPH + w][hd][d4 + 32 * k]);
+            A[k].x += ew[w] * v.x;
+            A[k].y += ew[w] * v.y;
+            A[k].z += ew[w] * v.z;
+            A[k].w += ew[w] * v.w;
           }
-          const int qh = (mt.h * HP + hh) * p.G + hd;
-          const int hs = hh * GPAD + hd;  // head slot in a segment record
+        }
+        const int qh = (mt.h * HP + hh) * p.G + hd;
+        const int hs = hh * GPAD + hd;  // head slot in a segment record
+        if (whole) {
+          float e, Lf;
+          sink_norm(L, M, p.s_aux, qh, &e, &Lf);
+          const long long ob = obase + static_cast<long long>(qh) * p.o_sh + d4;
 #pragma unroll
-          for (int dd = 0; dd < DPT; ++dd) {
-            const int d = et + dd * ETHREADS;
-            float A = 0.f;
-#pragma unroll
-            for (int w = 0; w < WPH; ++w) A += ew[w] * E.cacc[hh * WPH + w][hd][d];
-            if (whole)
-              store_out(p, obase + static_cast<long long>(qh) * p.o_sh + d, finalize(A, L, M, p.s_aux, qh, sv));
-            else
-              ws_acc[(static_cast<long long>(mt.seg) * GMAX + hs) * HEAD_DIM + d] = A;
+          for (int k = 0; k < 4; ++k) {
+            store_out(p, ob + 32 * k + 0, norm_out(A[k].x, e, Lf, sv));
+            store_out(p, ob + 32 * k + 1, norm_out(A[k].y, e, Lf, sv));
+            store_out(p, ob + 32 * k + 2, norm_out(A[k].z, e, Lf, sv));
+            store_out(p, ob + 32 * k + 3, norm_out(A[k].w, e, Lf, sv));
           }
-          if (!whole && et == 0) ws_ml[static_cast<long long>(mt.seg) * GMAX + hs] = make_float2(M, L);
+        } else {
+          float4* dst = reinterpret_cast<float4*>(&ws_acc[(static_cast<long long>(mt.seg) * GMAX + hs) * HEAD_DIM + d4]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) dst[8 * k] = A[k];
+          if ((u & 7) == 0) ws_ml[static_cast<long long>(mt.seg) * GMAX + hs] = make_float2(M, L);
         }
       }
       // the slot is consumed: give it back to the consumers
       mbar_arrive(smem_u32(&eempty[eb]));
+#ifdef FK_TRACE
+      if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][22] += gtimer() - te1;
+#endif
       if (++eb == C::NSLOT) {
         eb = 0;
         eph ^= 1u;
@@ -735,8 +810,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         }
         const int qh = (mt.h * HP + hh) * p.G + hd;
         const long long ob = obase + static_cast<long long>(qh) * p.o_sh + d0;
+        float e, Lf;
+        sink_norm(L, M, p.s_aux, qh, &e, &Lf);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) store_out(p, ob + i, finalize(A[i], L, M, p.s_aux, qh, sv));
+        for (int i = 0; i < 16; ++i) store_out(p, ob + i, norm_out(A[i], e, Lf, sv));
       }
       if (et == 0) cnt[item] = 0;
     }
@@ -952,7 +1029,14 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         l[0] += __shfl_xor_sync(0xffffffffu, l[0], o);
         l[1] += __shfl_xor_sync(0xffffffffu, l[1], o);
       }
-      if (!mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u)) {
+#ifdef FK_TRACE
+      const unsigned long long tq = gtimer();
+#endif
+      const bool eok = mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u);
+#ifdef FK_TRACE
+      if (threadIdx.x == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][21] += gtimer() - tq;
+#endif
+      if (!eok) {
         if (lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
         break;
       }
@@ -1259,6 +1343,10 @@ void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out
   p.scale_k = scale_k;
   p.scale_v = scale_v;
   p.ws = static_cast<unsigned char*>(ws);
+  p.q_al16 = (q_dtype != FK_DTYPE_E4M3 && (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (sq_b & 7) == 0 &&
+              (sq_h & 7) == 0)
+                 ? 1
+                 : 0;
 }
 
 }  // namespace fk
@@ -1557,6 +1645,6 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
 
 #ifdef FK_TRACE
 extern "C" int fk_trace_read(unsigned long long* host, int n) {
-  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 16 * n) == cudaSuccess ? 0 : 1;
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 24 * n) == cudaSuccess ? 0 : 1;
 }
 #endif

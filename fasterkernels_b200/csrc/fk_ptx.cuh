@@ -70,6 +70,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// ------------------------------------------------------------- cp.async
+// 16-byte asynchronous copy global -> shared (L2 only).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// The mbarrier tracks this thread's earlier cp.async copies: its pending
+// count rises by one now and falls by one when they have landed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ------------------------------------------------------------------- TMA
 // Plain tiled loads (no .multicast::cluster) into this CTA's shared memory,
 // completing on an mbarrier.
