@@ -1,4 +1,4 @@
-"""ctypes binding of the C-ABI in include/fk_decode.h, plus the per-device
+"""ctypes binding of the C-ABI in include/fk_decode.h, plus the per-stream
 workspace and the torch-tensor -> C-argument plumbing shared by the entry
 points.  torch supplies device memory and the current stream only; every
 decode runs in the sm_100a kernels of ``_lib/libfk_decode.so``.  There is no
@@ -127,41 +127,60 @@ _ws_lock = threading.Lock()
 
 
 def workspace(device: torch.device, batch: int, kv_heads: int, kv_dtype_code: int) -> torch.Tensor:
-    """The cached per-device workspace, grown to fit (batch, kv_heads).
+    """The cached workspace of (device, current stream), grown to fit
+    (batch, kv_heads).
 
-    Grown only outside CUDA-graph capture: a graph replays the pointer it
-    captured, so run one eager call with the largest batch before capturing.
-    Calls on one device share it, so they must be stream-ordered.
+    One workspace per stream: eager decode calls on different streams of a
+    device may run concurrently (their arrival counters and partials never
+    meet); calls on one stream are ordered by it.  Never allocated during
+    CUDA-graph capture: a graph replays the pointer it captured, so run one
+    eager call with the largest batch before capturing; a capture stream
+    without its own workspace adopts the device's largest one, so replay such
+    graphs in order with the eager calls of the warm-up stream.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
     need = int(lib().fk_decode_workspace_bytes(idx, batch, kv_heads, kv_dtype_code))
     if need == 0:
         raise RuntimeError(f"fk_decode_workspace_bytes failed: {last_error()}")
+    key = (idx, torch.cuda.current_stream(torch.device("cuda", idx)).cuda_stream)
     with _ws_lock:
-        ws = _ws.get(idx)
+        ws = _ws.get(key)
         if ws is None or ws.numel() < need:
             if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError(
-                    "decode workspace must be allocated before CUDA graph capture: run one eager "
-                    "decode call with the captured batch size first")
+                # torch.cuda.graph captures on a side stream: adopt the largest
+                # workspace the eager warm-up calls left on this device
+                fits = [w for (i, _), w in _ws.items() if i == idx and w.numel() >= need]
+                if not fits:
+                    raise RuntimeError(
+                        "decode workspace must be allocated before CUDA graph capture: run one eager "
+                        "decode call with the captured batch size first")
+                ws = max(fits, key=lambda w: w.numel())
+                _ws[key] = ws
+                return ws
             if ws is not None:
                 _ws_retired.append(ws)  # a captured graph may still point at it
             size = max(need, 0 if ws is None else ws.numel() * 2)
             ws = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
-            _ws[idx] = ws
+            _ws[key] = ws
         return ws
+
+
+def device_workspaces(device=None):
+    """The cached workspaces of a device (one per stream that decoded on it)."""
+    idx = torch.cuda.current_device() if device is None else torch.device(device).index
+    with _ws_lock:
+        return [w for (i, _), w in _ws.items() if i == idx]
 
 
 def read_status(device=None, clear: bool = True) -> int:
     """Read (and by default clear) the sticky FK_STATUS_* word of a device's
-    workspace.  Synchronises with the device; keep it off the hot path."""
-    idx = torch.cuda.current_device() if device is None else torch.device(device).index
-    ws = _ws.get(idx)
-    if ws is None:
-        return 0
-    st = int(ws[:4].view(torch.int32).item())
-    if clear:
-        ws[:4].zero_()
+    workspaces (OR over its streams).  Synchronises with the device; keep it
+    off the hot path."""
+    st = 0
+    for ws in device_workspaces(device):
+        st |= int(ws[:4].view(torch.int32).item())
+        if clear:
+            ws[:4].zero_()
     return st
 
 

@@ -128,8 +128,29 @@ def test_workspace_counters_rearmed(dev):
     for _ in range(3):
         fk.flash_decode_gqa_varlen(q, k, v, cu, s)
     torch.cuda.synchronize()
-    ws = N._ws[dev.index]
-    assert int(ws[256:256 + 4 * 3 * 8].view(torch.int32).abs().sum()) == 0
+    for ws in N.device_workspaces(dev):
+        assert int(ws[256:256 + 4 * 3 * 8].view(torch.int32).abs().sum()) == 0
+
+
+def test_concurrent_streams_have_separate_workspaces(dev):
+    # decode calls on two streams run concurrently: each stream has its own
+    # workspace, so split-item counters and partials never collide
+    cases = [_rand_case(dev, [20000, 9000, 31000, 4000], 32, 8, torch.float16, True, seed=70 + i) for i in range(2)]
+    refs = [fk.flash_decode_gqa_varlen(*c) for c in cases]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(dev) for _ in cases]
+    for st in streams:
+        st.wait_stream(torch.cuda.current_stream(dev))
+    outs = [[], []]
+    for _ in range(6):
+        for i, (st, c) in enumerate(zip(streams, cases)):
+            with torch.cuda.stream(st):
+                outs[i].append(fk.flash_decode_gqa_varlen(*c))
+    torch.cuda.synchronize()
+    for i in range(2):
+        for o in outs[i]:
+            assert torch.equal(o, refs[i])
+    assert len(N.device_workspaces(dev)) >= 3
 
 
 def test_workspace_shared_across_shapes(dev):
