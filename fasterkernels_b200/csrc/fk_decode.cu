@@ -43,6 +43,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <string>
 
 #include "../../include/fk_decode.h"
@@ -1262,6 +1263,48 @@ inline bool pdl_enabled() {
   return on;
 }
 
+// A decode kernel launched as a programmatic dependent may start while the
+// previous decode kernel of its stream still runs; only its epilogue warps
+// wait for that grid.  Its producer reads Q, the lengths and the block table
+// at once, so a call whose inputs overlap the previous call's output (out
+// fed back as q) is launched without the attribute.  One record per stream.
+struct ByteRange {
+  uintptr_t lo = 0, hi = 0;
+  bool overlaps(const ByteRange& o) const { return lo < o.hi && o.lo < hi; }
+};
+std::mutex g_last_out_mu;
+std::unordered_map<cudaStream_t, ByteRange> g_last_out;
+
+ByteRange span(const void* base, long long last_elem, size_t es) {
+  ByteRange r;
+  if (base == nullptr) return r;
+  r.lo = reinterpret_cast<uintptr_t>(base);
+  r.hi = r.lo + static_cast<uintptr_t>(last_elem + 1) * es;
+  return r;
+}
+
+bool pdl_safe(const Params& p, cudaStream_t stream) {
+  const size_t q_es = (p.q_dtype == FK_DTYPE_E4M3) ? 1 : 2;
+  const long long qh = static_cast<long long>(p.q_heads) - 1, b = static_cast<long long>(p.B) - 1;
+  const ByteRange in[7] = {
+      span(p.q, b * p.q_sb + qh * p.q_sh + HEAD_DIM - 1, q_es),
+      span(p.lens, p.B, 4),
+      span(p.starts, b, 4),
+      span(p.bt, b * p.bt_sb + p.max_blocks - 1, 4),
+      span(p.scale_q, 0, 4),
+      span(p.scale_k, 0, 4),
+      span(p.s_aux, qh, 4)};
+  const ByteRange out = span(p.out, b * p.o_sb + qh * p.o_sh + HEAD_DIM - 1, 2);
+  std::lock_guard<std::mutex> lk(g_last_out_mu);
+  auto it = g_last_out.find(stream);
+  bool safe = true;
+  if (it != g_last_out.end())
+    for (const ByteRange& r : in)
+      if (r.hi > r.lo && r.overlaps(it->second)) safe = false;
+  g_last_out[stream] = out;
+  return safe;
+}
+
 template <int KV, int LAYOUT, int HP>
 int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
   const int rc = prepare_kernel<KV, LAYOUT, HP>(device);
@@ -1273,7 +1316,7 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = (pdl_enabled() && pdl_safe(p, stream)) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP>, p);

@@ -378,6 +378,29 @@ def test_back_to_back_calls_overlapping_launches(dev):
     assert N.read_status(dev) == 0
 
 
+def test_chained_calls_output_fed_back_as_query(dev):
+    # one call's output is the next call's query on the same stream: the
+    # second launch must not start reading q before the first has written it
+    q, k, v, cu, s = _rand_case(dev, [30000, 12000, 25000, 9000], 32, 8, torch.float16, True, seed=44)
+    outs = [q]
+    for _ in range(4):
+        outs.append(fk.flash_decode_gqa_varlen(outs[-1], k, v, cu, s))
+    torch.cuda.synchronize()
+    for i in range(1, len(outs)):
+        close(outs[i], _oracle(outs[i - 1], k, v, cu, s), **F16_TOL)
+    # the same with a single buffer updated in place through out=
+    x = q.clone()
+    ref = q.clone()
+    y = torch.empty_like(x)
+    for _ in range(3):
+        fk.flash_decode_gqa_varlen(x, k, v, cu, s, out=y)
+        fk.flash_decode_gqa_varlen(y, k, v, cu, s, out=x)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        ref = torch.from_numpy(_oracle(torch.from_numpy(_oracle(ref, k, v, cu, s)).to(dev).half(), k, v, cu, s)).to(dev).half()
+    close(x, ref.float().cpu().numpy(), atol=5e-3, rtol=2e-2)
+
+
 @pytest.mark.parametrize("pool_dtype", [torch.float16, torch.bfloat16, torch.float8_e4m3fn])
 def test_paged_kv_append_matches_torch(dev, pool_dtype):
     B, KVH, P = 5, 8, 40
