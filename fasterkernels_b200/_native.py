@@ -56,6 +56,8 @@ def lib() -> ctypes.CDLL:
         L.fk_last_error.argtypes = []
         L.fk_decode_workspace_bytes.restype = _Z
         L.fk_decode_workspace_bytes.argtypes = [_I, _I, _I, _I]
+        L.fk_decode_workspace_bytes_gqa.restype = _Z
+        L.fk_decode_workspace_bytes_gqa.argtypes = [_I, _I, _I, _I, _I]
         L.fk_flash_decode_gqa_varlen.restype = _I
         L.fk_flash_decode_gqa_varlen.argtypes = [
             _P, _P, _P, _P, _P, _P,          # q k v cu s_aux out
@@ -126,9 +128,9 @@ _ws_retired = []
 _ws_lock = threading.Lock()
 
 
-def workspace(device: torch.device, batch: int, kv_heads: int, kv_dtype_code: int) -> torch.Tensor:
+def workspace(device: torch.device, batch: int, q_heads: int, kv_heads: int, kv_dtype_code: int) -> torch.Tensor:
     """The cached workspace of (device, current stream), grown to fit
-    (batch, kv_heads).
+    (batch, q_heads, kv_heads).
 
     One workspace per stream: eager decode calls on different streams of a
     device may run concurrently (their arrival counters and partials never
@@ -139,9 +141,9 @@ def workspace(device: torch.device, batch: int, kv_heads: int, kv_dtype_code: in
     graphs in order with the eager calls of the warm-up stream.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    need = int(lib().fk_decode_workspace_bytes(idx, batch, kv_heads, kv_dtype_code))
+    need = int(lib().fk_decode_workspace_bytes_gqa(idx, batch, q_heads, kv_heads, kv_dtype_code))
     if need == 0:
-        raise RuntimeError(f"fk_decode_workspace_bytes failed: {last_error()}")
+        raise RuntimeError(f"fk_decode_workspace_bytes_gqa failed: {last_error()}")
     key = (idx, torch.cuda.current_stream(torch.device("cuda", idx)).cuda_stream)
     with _ws_lock:
         ws = _ws.get(key)

@@ -22,7 +22,8 @@
 // loads (64 tokens x 128 dims of K and of V per stage, 128-byte swizzled)
 // into an mbarrier ring; four consumer warps each take 16 tokens of every
 // tile and run QK^T and PV on the tensor cores with mma.sync m16n8k16,
-// tokens as the M dimension and the G <= 8 query heads of the KV group as N,
+// tokens as the M dimension and up to 8 query heads of the KV group as N (a
+// larger group is split into items of at most 8 query heads),
 // keeping a private online-softmax state that is merged across the warps at
 // the end of each segment.  FP8 e4m3 K/V are widened to f16 in registers;
 // scale_k folds into the logit scale and scale_v into the final output.
@@ -183,7 +184,48 @@ struct Params {
   int q_dtype, out_dtype;
   int num_ctas;
   int q_al16;  // q base and strides 16-byte aligned (rows can be copied with cp.async)
+  int qc;      // query chunks of at most 8 heads per KV head: ceil(G / 8)
 };
+
+// Work items of a sequence and their two head slots hh < HP (an MMA N of 8
+// query heads each).  A group of up to 8 query heads (qc = 1): item hi covers
+// KV heads hi*HP .. + HP - 1, slot hh holds the group of KV head hi*HP + hh.
+// Larger groups are cut into qc chunks of at most 8 query heads: with HP = 2
+// the two slots of an item hold two chunks of ONE KV head, whose tile is
+// loaded once and read by both slots' warps ("chunk pairs"); with HP = 1 each
+// chunk is an item.  Slot hh holds query heads item_q(hi, hh, j) of KV head
+// item_kv(hi), j < item_g(hi, hh) (0 for the empty second slot of an odd
+// chunk count).
+template <int HP>
+__device__ __forceinline__ bool chunk_pairs(const Params& p) {
+  return HP == 2 && p.qc > 1;
+}
+template <int HP>
+__device__ __forceinline__ int item_kv(const Params& p, int hi) {
+  if (p.qc == 1) return hi * HP;
+  return HP == 2 ? hi / ((p.qc + 1) >> 1) : hi / p.qc;
+}
+template <int HP>
+__device__ __forceinline__ int item_chunk(const Params& p, int hi, int hh) {
+  if (p.qc == 1) return 0;
+  return HP == 2 ? (hi % ((p.qc + 1) >> 1)) * 2 + hh : hi % p.qc;
+}
+template <int HP>
+__device__ __forceinline__ int item_q(const Params& p, int hi, int hh, int j) {
+  if (p.qc == 1) return (hi * HP + hh) * p.G + j;
+  return item_kv<HP>(p, hi) * p.G + item_chunk<HP>(p, hi, hh) * 8 + j;
+}
+template <int HP>
+__device__ __forceinline__ int item_g(const Params& p, int hi, int hh) {
+  if (p.qc == 1) return p.G;
+  return max(0, min(8, p.G - item_chunk<HP>(p, hi, hh) * 8));
+}
+// Items per sequence.
+template <int HP>
+__device__ __forceinline__ int items_per_seq(const Params& p) {
+  if (p.qc == 1) return p.kv_heads / HP;
+  return HP == 2 ? p.kv_heads * ((p.qc + 1) >> 1) : p.kv_heads * p.qc;
+}
 
 // Effective length of sequence b and the coordinate of its first token.
 template <int LAYOUT>
@@ -310,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   int* cnt = reinterpret_cast<int*>(p.ws + p.ws_cnt);
   float2* ws_ml = reinterpret_cast<float2*>(p.ws + p.ws_ml);
   float* ws_acc = reinterpret_cast<float*>(p.ws + p.ws_acc);
-  const int KVI = p.kv_heads / HP;  // items per sequence
+  const int KVI = items_per_seq<HP>(p);
   __shared__ int s_last;
 
 #ifdef FK_TRACE
@@ -340,11 +382,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   // stage's full barrier with the KV tiles; the padding rows (heads G..7) are
   // zeroed once, here.  Otherwise the producer converts Q through registers.
   const bool q_async = p.q_al16 && p.q_dtype == (C::BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16);
-  if (q_async && p.G < GPAD) {
-    const int npad = GPAD - p.G;
+  // fewest query heads in a slot of any item
+  const int gmin = p.qc == 1 ? p.G : (chunk_pairs<HP>(p) && (p.qc & 1)) ? 0 : (p.G % 8 == 0 ? 8 : p.G % 8);
+  if (q_async && gmin < GPAD) {
+    const int npad = GPAD - gmin;
     for (int u = threadIdx.x; u < C::STAGES * HP * npad * 16; u += THREADS) {
       const int row = u >> 4, c = u & 15;  // row over (stage, head, padding head)
-      const int sh = row / npad, j = p.G + row % npad;
+      const int sh = row / npad, j = gmin + row % npad;
       reinterpret_cast<uint4*>(qstage + sh * (GPAD * 64) + j * 64)[c] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
@@ -433,8 +477,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       for (int k = 0; k < QW; ++k) {
         const int idx = lane + 32 * k;
         const int hh = idx / (GPAD * 64), j = (idx >> 6) & (GPAD - 1), d = (idx & 63) * 2;
-        const int qh = (ih * HP + hh) * p.G + j;
-        qpre[k] = (j < p.G) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d) : 0u;
+        const int qh = item_q<HP>(p, ih, hh, j);
+        qpre[k] = (j < item_g<HP>(p, ih, hh)) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d) : 0u;
       }
       qpre_b = bb;
       qpre_h = ih;
@@ -492,7 +536,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         const int nseg = static_cast<int>((item_base + nb - 1) / per) - c0 + 1;
         const int tbeg = g0 * PAGE;
         const int tend = min(g1 * PAGE, len);
-        const int hcoord = hi * HP;  // first KV head of the item
+        const int hcoord = item_kv<HP>(p, hi);  // first KV head of the item
 #ifdef FK_TRACE
         unsigned long long tr_sw0 = gtimer();
 #endif
@@ -512,7 +556,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           const uint32_t sV = sK + C::TILE_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
           int bad = 0;
-          uint32_t bytes = 2u * C::TILE_BYTES;
+          // chunk pairs load one KV head: half a stage
+          const uint32_t nkv = chunk_pairs<HP>(p) ? 1u : static_cast<uint32_t>(HP);
+          uint32_t bytes = 2u * C::TILE_BYTES / HP * nkv;
           int phys = -1;
           if constexpr (LAYOUT == PAGED) {
             const int p0 = tt / PAGE;
@@ -532,7 +578,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
             const bool okp = (lane < np) && phys >= 0 && phys < p.num_pages;
             const unsigned okm = __ballot_sync(0xffffffffu, okp) & ((1u << PPT) - 1u);
             bad = static_cast<int>(~okm & ((1u << np) - 1u));
-            bytes = static_cast<uint32_t>(__popc(okm)) * 2u * HP * C::PAGE_BYTES;
+            bytes = static_cast<uint32_t>(__popc(okm)) * 2u * nkv * C::PAGE_BYTES;
             if (lane == 0 && bad) atomicOr(&hdr->status, FK_STATUS_BAD_PAGE);
             if (!okp) phys = -1;
           }
@@ -546,9 +592,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
               // the item's HP*G rows of 256 bytes, 16 bytes per copy
               const uint32_t qd = smem_u32(qs);
               const long long qb0 = static_cast<long long>(b) * p.q_sb;
-              for (int u = lane; u < HP * p.G * 16; u += 32) {
-                const int hh = u / (p.G * 16), j = (u >> 4) % p.G, c = u & 15;
-                const int qh = (hi * HP + hh) * p.G + j;
+              const int g0 = item_g<HP>(p, hi, 0), g1 = HP == 2 ? item_g<HP>(p, hi, 1) : 0;
+              for (int u = lane; u < (g0 + g1) * 16; u += 32) {
+                const int r = u >> 4, c = u & 15;
+                const int hh = r < g0 ? 0 : 1, j = r < g0 ? r : r - g0;
+                const int qh = item_q<HP>(p, hi, hh, j);
                 cp_async16(qd + (hh * GPAD + j) * 256 + c * 16,
                            static_cast<const unsigned short*>(p.q) + qb0 + static_cast<long long>(qh) * p.q_sh + c * 8);
               }
@@ -705,8 +753,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       // One unit per thread and round: query head hd of KV head hh (head
       // slot u / 8), dims (u % 8) * 4 + 32 k, k < 4 (a quarter warp reads
       // 128 contiguous bytes of the slot: no bank conflicts).
-      for (int u = et; u < HP * p.G * 8; u += ETHREADS) {
-        const int hh = u / (p.G * 8), hd = (u >> 3) % p.G, d4 = (u & 7) * 4;
+      const int g0 = item_g<HP>(p, mt.h, 0), g1 = HP == 2 ? item_g<HP>(p, mt.h, 1) : 0;
+      for (int u = et; u < (g0 + g1) * 8; u += ETHREADS) {
+        const int r = u >> 3, d4 = (u & 7) * 4;
+        const int hh = r < g0 ? 0 : 1, hd = r < g0 ? r : r - g0;
         float M = NEG_INF;
 #pragma unroll
         for (int w = 0; w < WPH; ++w) M = fmaxf(M, E.cm[hh * WPH + w][hd]);
@@ -730,7 +780,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
             A[k].w += ew[w] * v.w;
           }
         }
-        const int qh = (mt.h * HP + hh) * p.G + hd;
+        const int qh = item_q<HP>(p, mt.h, hh, hd);
         const int hs = hh * GPAD + hd;  // head slot in a segment record
         if (whole) {
           float e, Lf;
@@ -768,8 +818,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       __threadfence();
       // All head slots in parallel: unit u = (slot u / 8, dims (u % 8) * 16 ..
       // +16); each thread merges its units with 4 segments' loads in flight.
-      for (int u = et; u < HP * p.G * 8; u += ETHREADS) {
-        const int hh = u / (p.G * 8), hd = (u / 8) % p.G, d0 = (u % 8) * 16;
+      for (int u = et; u < (g0 + g1) * 8; u += ETHREADS) {
+        const int r = u >> 3, d0 = (u & 7) * 16;
+        const int hh = r < g0 ? 0 : 1, hd = r < g0 ? r : r - g0;
         const int hs = hh * GPAD + hd;
         float M = NEG_INF, L = 0.f;
         float A[16];
@@ -809,7 +860,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           }
           M = Mn;
         }
-        const int qh = (mt.h * HP + hh) * p.G + hd;
+        const int qh = item_q<HP>(p, mt.h, hh, hd);
         const long long ob = obase + static_cast<long long>(qh) * p.o_sh + d0;
         float e, Lf;
         sink_norm(L, M, p.s_aux, qh, &e, &Lf);
@@ -829,7 +880,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   constexpr bool MBF16 = C::BF16;  // MMA element type (FP8 KV computes in f16)
   const int g = lane >> 2;
   const int t = lane & 3;
-  const int hh = warp / WPH;            // KV head of the item this warp serves
+  const int hh = warp / WPH;            // head slot of the item this warp serves
+  const int hk = chunk_pairs<HP>(p) ? 0 : hh;  // its KV head's tile in the stage
   const int r0 = (warp % WPH) * 16;      // its 16 rows of that head's tile
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
@@ -915,7 +967,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         rowA = prow;
         rowB = prow + 8;
         const int sw = prow & 7;
-        const uint32_t ra = sK + TL::row_off(hh, prow), rb = ra + 8 * 128;
+        const uint32_t ra = sK + TL::row_off(hk, prow), rb = ra + 8 * 128;
         const uint4 alo = lds128(ra + ((t ^ sw) << 4));
         const uint4 ahi = lds128(ra + (((t + 4) ^ sw) << 4));
         const uint4 blo = lds128(rb + ((t ^ sw) << 4));
@@ -934,7 +986,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       } else {
         rowA = r0 + g;
         rowB = r0 + g + 8;
-        const uint32_t kb = sK + TL::row_off(hh, krow);
+        const uint32_t kb = sK + TL::row_off(hk, krow);
         const int ksw = krow & 7;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -987,7 +1039,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const int row = r0 + t + 4 * (r & 1) + 8 * (r >> 1);
-          x[r] = lds128(sV + TL::row_off(hh, row) + ((cg ^ (row & 7)) << 4));
+          x[r] = lds128(sV + TL::row_off(hk, row) + ((cg ^ (row & 7)) << 4));
           if (partial && !tok_ok(row)) x[r] = make_uint4(0u, 0u, 0u, 0u);
         }
         const uint32_t w0[4] = {x[0].x, x[0].y, x[0].z, x[0].w};
@@ -1009,7 +1061,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           mk01 = (tok_ok(tk) ? 0x0000ffffu : 0u) | (tok_ok(tk + 1) ? 0xffff0000u : 0u);
           mk89 = (tok_ok(tk + 8) ? 0x0000ffffu : 0u) | (tok_ok(tk + 9) ? 0xffff0000u : 0u);
         }
-        const uint32_t vb = sV + TL::row_off(hh, vrow);
+        const uint32_t vb = sV + TL::row_off(hk, vrow);
         const int vsw = vrow & 7;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -1132,17 +1184,32 @@ constexpr size_t smem_bytes() {
          C::NSLOT * (sizeof(EpiSlot) + sizeof(Meta) + 2 * sizeof(uint64_t));
 }
 
+// Query chunks per KV head: groups of more than 8 query heads are split into
+// items of at most 8 (the MMA N), each reading its KV head.
+inline int qc_for(int q_heads, int kv_heads) {
+  const int g = (kv_heads > 0) ? q_heads / kv_heads : 1;
+  return g > 8 ? (g + 7) / 8 : 1;
+}
+
 // KV heads per work item: 2 when kv_heads is even (one TMA box then covers
-// both heads of a page), else 1.  FK_DECODE_HP=1 in the environment forces
-// single-head items (a tuning knob; read once, applies to every layout so
-// paged and contiguous results stay bit-identical).
-inline int hp_for(int kv_heads) {
+// both heads of a page) and the group fits one item, else 1.
+// FK_DECODE_HP=1 in the environment forces single-head items (a tuning knob;
+// read once, applies to every layout so paged and contiguous results stay
+// bit-identical).
+inline int hp_for(int kv_heads, int qc = 1) {
   static const int forced = [] {
     const char* e = getenv("FK_DECODE_HP");
     return (e != nullptr && e[0] == '1') ? 1 : 0;
   }();
   if (forced == 1) return 1;
+  if (qc > 1) return 2;  // chunk pairs of one KV head
   return (kv_heads % 2 == 0) ? 2 : 1;
+}
+
+// KV heads in one TMA box: chunk pairs load a single head.
+inline uint32_t box_heads(int kv_heads, int qc) {
+  const int hp = hp_for(kv_heads, qc);
+  return static_cast<uint32_t>((qc > 1) ? 1 : hp);
 }
 
 template <int KV, int LAYOUT, int HP>
@@ -1233,8 +1300,6 @@ int common_checks(const void* q, const void* k, const void* v, const void* out, 
   if (head_dim != HEAD_DIM) return fail(FK_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
   if (q_heads % kv_heads != 0)
     return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a multiple of kv_heads (%d)", q_heads, kv_heads);
-  if (q_heads / kv_heads > GPAD)
-    return fail(FK_ERR_UNSUPPORTED, "GQA group size %d > %d is not supported", q_heads / kv_heads, GPAD);
   if (!is16(out_dtype)) return fail(FK_ERR_UNSUPPORTED, "out dtype must be f16 or bf16");
   if (kv_dtype != FK_DTYPE_E4M3 && !is16(kv_dtype)) return fail(FK_ERR_UNSUPPORTED, "unsupported kv dtype %d", kv_dtype);
   if (q_dtype != FK_DTYPE_E4M3 && !is16(q_dtype)) return fail(FK_ERR_UNSUPPORTED, "unsupported q dtype %d", q_dtype);
@@ -1326,14 +1391,15 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
 
 template <int LAYOUT>
 int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) {
-  const int hp = hp_for(p.kv_heads);
+  const int hp = hp_for(p.kv_heads, p.qc);
   const int S = num_work_ctas(device, kv, hp);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   p.num_ctas = S;
-  const WsLayout wl(ws_bytes, p.B, p.kv_heads, S);
-  if (!wl.fits(ws_bytes, p.B, p.kv_heads))
+  const int kvq = p.kv_heads * p.qc;  // (KV head, query chunk) pairs per sequence
+  const WsLayout wl(ws_bytes, p.B, kvq, S);
+  if (!wl.fits(ws_bytes, p.B, kvq))
     return fail(FK_ERR_WORKSPACE, "workspace too small: %zu bytes < %zu required", ws_bytes,
-                WsLayout::min_bytes(p.B, p.kv_heads, S));
+                WsLayout::min_bytes(p.B, kvq, S));
   p.ws_cnt = static_cast<long long>(wl.cnt);
   p.ws_ml = static_cast<long long>(wl.ml);
   p.ws_acc = static_cast<long long>(wl.acc);
@@ -1386,6 +1452,7 @@ void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out
   p.scale_k = scale_k;
   p.scale_v = scale_v;
   p.ws = static_cast<unsigned char*>(ws);
+  p.qc = qc_for(q_heads, kv_heads);
   p.q_al16 = (q_dtype != FK_DTYPE_E4M3 && (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (sq_b & 7) == 0 &&
               (sq_h & 7) == 0)
                  ? 1
@@ -1403,17 +1470,22 @@ extern "C" int fk_version(void) { return 100; }
 
 extern "C" const char* fk_last_error(void) { return g_err.c_str(); }
 
-extern "C" size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads, int kv_dtype) {
-  if (batch < 0 || kv_heads <= 0) {
+extern "C" size_t fk_decode_workspace_bytes_gqa(int device, int batch, int q_heads, int kv_heads, int kv_dtype) {
+  if (batch < 0 || kv_heads <= 0 || q_heads <= 0 || q_heads % kv_heads != 0) {
     fail(FK_ERR_INVALID_ARG, "bad sizes");
     return 0;
   }
-  const int S = num_work_ctas(device, kv_dtype, hp_for(kv_heads));
+  const int qc = qc_for(q_heads, kv_heads);
+  const int S = num_work_ctas(device, kv_dtype, hp_for(kv_heads, qc));
   if (S <= 0) {
     fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
     return 0;
   }
-  return WsLayout::min_bytes(batch, kv_heads, S);
+  return WsLayout::min_bytes(batch, kv_heads * qc, S);
+}
+
+extern "C" size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads, int kv_dtype) {
+  return fk_decode_workspace_bytes_gqa(device, batch, kv_heads, kv_heads, kv_dtype);
 }
 
 extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, const void* v_varlen,
@@ -1439,11 +1511,12 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
               nullptr, workspace);
   p.lens = cu_seqlens_k;
   const uint64_t T = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
-  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads));
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
+  const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
   // 16-bit rows as (64 dims, T rows, 2 halves [128 B apart], heads): one box
   // {64, 64/hp, 2, hp} per stage lands as [head][half][rows][64].
   const uint64_t dims[4] = {64, T, 2, static_cast<uint64_t>(kv_heads)};
-  const uint32_t box[4] = {64, TILE / hp, 2, hp};
+  const uint32_t box[4] = {64, TILE / hp, 2, hb};
   const uint64_t ks[3] = {static_cast<uint64_t>(sk_t) * 2, 128, static_cast<uint64_t>(sk_h) * 2};
   const uint64_t vs[3] = {static_cast<uint64_t>(sv_t) * 2, 128, static_cast<uint64_t>(sv_h) * 2};
   if ((rc = encode_map(&p.tk, dtype, 4, k_varlen, dims, ks, box)) != FK_OK) return rc;
@@ -1478,12 +1551,13 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
   p.lens = cache_lens;
   p.starts = start_k_offsets;
   p.max_tokens = max_seqlen;
-  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads));
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
+  const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
   const uint64_t Bd = static_cast<uint64_t>(batch > 0 ? batch : 1);
   if (kv_dtype == FK_DTYPE_E4M3) {
     // (128 dims, S rows, heads, batch): box {128, 64/hp, hp, 1} -> [head][rows][128]
     const uint64_t dims[4] = {HEAD_DIM, static_cast<uint64_t>(max_seqlen), static_cast<uint64_t>(kv_heads), Bd};
-    const uint32_t box[4] = {128, TILE / hp, hp, 1};
+    const uint32_t box[4] = {128, TILE / hp, hb, 1};
     const uint64_t ks[3] = {static_cast<uint64_t>(sk_s), static_cast<uint64_t>(sk_h), static_cast<uint64_t>(sk_b)};
     const uint64_t vs[3] = {static_cast<uint64_t>(sv_s), static_cast<uint64_t>(sv_h), static_cast<uint64_t>(sv_b)};
     if ((rc = encode_map(&p.tk, kv_dtype, 4, k_cache, dims, ks, box)) != FK_OK) return rc;
@@ -1491,7 +1565,7 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
   } else {
     // (64 dims, S rows, 2 halves, heads, batch): box {64, 64/hp, 2, hp, 1} -> [head][half][rows][64]
     const uint64_t dims[5] = {64, static_cast<uint64_t>(max_seqlen), 2, static_cast<uint64_t>(kv_heads), Bd};
-    const uint32_t box[5] = {64, TILE / hp, 2, hp, 1};
+    const uint32_t box[5] = {64, TILE / hp, 2, hb, 1};
     const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
                             static_cast<uint64_t>(sk_b) * 2};
     const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
@@ -1535,11 +1609,12 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   p.bt_sb = bt_b;
   p.max_blocks = max_blocks;
   p.num_pages = static_cast<int>(num_pages);
-  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads));
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
+  const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
   if (kv_dtype == FK_DTYPE_E4M3) {
     // [P, KVH, 16, 128] bytes: one box {128, 16, hp, 1} per page -> [head][16][128]
     const uint64_t dims[4] = {HEAD_DIM, PAGE, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
-    const uint32_t box[4] = {128, PAGE, hp, 1};
+    const uint32_t box[4] = {128, PAGE, hb, 1};
     const uint64_t ks[3] = {static_cast<uint64_t>(sk_s), static_cast<uint64_t>(sk_h), static_cast<uint64_t>(sk_p)};
     const uint64_t vs[3] = {static_cast<uint64_t>(sv_s), static_cast<uint64_t>(sv_h), static_cast<uint64_t>(sv_p)};
     if ((rc = encode_map(&p.tk, kv_dtype, 4, k_pool, dims, ks, box)) != FK_OK) return rc;
@@ -1549,7 +1624,7 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
     // the third dimension (stride 128 B), so one box {64, 16, 2, hp} carries a
     // page for the item's heads and lands as [head][half][16 rows][64 dims].
     const uint64_t dims[5] = {64, PAGE, 2, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
-    const uint32_t box[5] = {64, PAGE, 2, hp, 1};
+    const uint32_t box[5] = {64, PAGE, 2, hb, 1};
     const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
                             static_cast<uint64_t>(sk_p) * 2};
     const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
@@ -1660,9 +1735,12 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
   }
   const int device = attr.device;
   if (batch < 0 || kv_heads <= 0) return fail(FK_ERR_INVALID_ARG, "bad sizes: batch=%d kv_heads=%d", batch, kv_heads);
-  const int S = num_work_ctas(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp_for(kv_heads));
+  if (q_heads <= 0 || q_heads % kv_heads != 0)
+    return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a positive multiple of kv_heads (%d)", q_heads, kv_heads);
+  const int qc = qc_for(q_heads, kv_heads);
+  const int S = num_work_ctas(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp_for(kv_heads, qc));
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
-  const size_t need = WsLayout::min_bytes(batch, kv_heads, S);
+  const size_t need = WsLayout::min_bytes(batch, kv_heads * qc, S);
   if (need > NOALLOC_SCRATCH_BYTES)
     return fail(FK_ERR_WORKSPACE,
                 "batch*kv_heads = %lld needs %zu bytes of scratch; the allocation-free entry point has a fixed "
@@ -1674,7 +1752,7 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
   if (rc != FK_OK) return rc;
   // The status word and the arrival counters must start at zero: clear them on
   // the caller's stream (a memset, not an allocation).
-  const WsLayout wl(NOALLOC_SCRATCH_BYTES, batch, kv_heads, S);
+  const WsLayout wl(NOALLOC_SCRATCH_BYTES, batch, kv_heads * qc, S);
   int prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);

@@ -82,7 +82,7 @@ def flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux=None, *, 
     elif out.shape != (B, QH, D) or out.dtype != q.dtype or out.stride(-1) != 1:
         raise ValueError("out must be [B, Q_H, 128] of q's dtype with unit inner stride")
     code = N.dtype_code(q.dtype)
-    ws = N.workspace(dev, B, KVH, code)
+    ws = N.workspace(dev, B, QH, KVH, code)
     rc = N.lib().fk_flash_decode_gqa_varlen(
         N.ptr(q), N.ptr(k_varlen), N.ptr(v_varlen), N.ptr(cu), N.ptr(s_aux), N.ptr(out),
         B, QH, KVH, D, T, code,

@@ -89,7 +89,7 @@ def dense_decode(q, k_cache, v_cache, cache_lens, start_k_offsets=None, *, s_aux
         out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
         raise ValueError("out must be [B, Q_H, 128] of out_dtype with unit inner stride")
-    ws = N.workspace(dev, B, KVH, kv_code)
+    ws = N.workspace(dev, B, QH, KVH, kv_code)
     rc = N.lib().fk_flash_decode_gqa_hf_dense(
         N.ptr(q), N.ptr(k_cache), N.ptr(v_cache), N.ptr(lens), N.ptr(starts), N.ptr(s_aux), N.ptr(out),
         B, QH, KVH, D, S, q_code, kv_code, out_code, N.ptr(sq), N.ptr(sk), N.ptr(sv),

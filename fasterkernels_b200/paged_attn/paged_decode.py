@@ -63,7 +63,7 @@ def paged_flash_decode(q, k_pool, v_pool, block_table, seq_lens, page_size, *, s
         out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
         raise ValueError("out must be [B, Q_H, 128] of out_dtype with unit inner stride")
-    ws = N.workspace(dev, B, KVH, kv_code)
+    ws = N.workspace(dev, B, QH, KVH, kv_code)
     rc = N.lib().fk_paged_flash_decode(
         N.ptr(q), N.ptr(k_pool), N.ptr(v_pool), N.ptr(bt), N.ptr(lens), N.ptr(s_aux), N.ptr(out),
         B, QH, KVH, D, P, PS, bt.shape[1], q_code, kv_code, out_code, N.ptr(sq), N.ptr(sk), N.ptr(sv),

@@ -62,10 +62,17 @@ int fk_version(void);
 const char* fk_last_error(void);
 
 /*
- * Bytes of workspace an entry point needs for `batch` sequences and
- * `kv_heads` KV heads with KV element type `kv_dtype`, on `device`.
- * Returns 0 on error (see fk_last_error()).
+ * Bytes of workspace an entry point needs for `batch` sequences, `q_heads`
+ * query heads and `kv_heads` KV heads with KV element type `kv_dtype`, on
+ * `device`.  Any GQA group size q_heads / kv_heads is accepted, as the
+ * reference's Triton kernels accept any (they pad the group to BLOCK_H =
+ * max(16, next_pow2(G)), fskernels/triton/triton_gqa_decode.py:132): a group
+ * of more than 8 query heads is processed in chunks of at most 8, which
+ * needs more workspace.  Returns 0 on error (see fk_last_error()).
  */
+size_t fk_decode_workspace_bytes_gqa(int device, int batch, int q_heads, int kv_heads, int kv_dtype);
+
+/* The same for group sizes q_heads / kv_heads <= 8. */
 size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads, int kv_dtype);
 
 /*

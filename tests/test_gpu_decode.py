@@ -562,3 +562,55 @@ def test_paged_strided_block_table(dev):
     out = fk.paged_flash_decode(q, kp, vp, wide[:, : bt.shape[1] + 3], torch.tensor(lens, dtype=torch.int32,
                                                                                      device=dev), 16, s_aux=s)
     assert torch.equal(out, fk.flash_decode_gqa_varlen(q, k, v, cu, s))
+
+
+# ------------------------------------------------- groups of more than 8 heads
+# The reference's Triton kernels take any group size (BLOCK_H pads it,
+# fskernels/triton/triton_gqa_decode.py:132); here a group of more than 8
+# query heads is split into items of at most 8 sharing the KV head.
+@pytest.mark.parametrize("G,kvh", [(9, 4), (12, 8), (16, 8), (32, 2)])
+@pytest.mark.parametrize("sinks", [False, True])
+def test_varlen_large_groups(dev, G, kvh, sinks):
+    lens = [1, 17, 64, 700, 0, 5000, 12345]
+    q, k, v, cu, s = _rand_case(dev, lens, G * kvh, kvh, torch.float16, sinks, seed=80 + G)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(out, _oracle(q, k, v, cu, s), **F16_TOL)
+    assert N.read_status(dev) == 0
+
+
+def test_large_group_bf16_paged_matches_varlen_bitwise(dev):
+    lens = [3000, 1, 16, 9000, 257]
+    q, k, v, cu, s = _rand_case(dev, lens, 128, 8, torch.bfloat16, True, seed=91)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(out, _oracle(q, k, v, cu, s), **BF16_TOL)
+    kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.25, seed=3)
+    outp = fk.paged_flash_decode(q, kp, vp, bt, torch.tensor(lens, dtype=torch.int32, device=dev), 16, s_aux=s)
+    assert torch.equal(out, outp)
+
+
+@pytest.mark.parametrize("G", [12, 16])
+def test_fp8_large_groups_paged_and_dense(dev, G):
+    lens = [1, 33, 1500, 0, 4097]
+    kvh = 4
+    d = W.make_varlen(lens, G * kvh, kvh, torch.float32, dev, seed=60 + G, sinks=True)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    q = d["q"].half()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=G)
+    outp = fk.paged_flash_decode(q, kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn), bt, sl, 16,
+                                 s_aux=d["s_aux"], scale_k=sk, scale_v=sv)
+    ref = O.decode_varlen(q.float().cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
+                          d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
+    close(outp, ref, atol=3e-3, rtol=1e-2)
+    # the HF dense cache [B, KVH, S, D] with the same tokens
+    S = max(lens)
+    kc = torch.zeros(len(lens), kvh, S, 128, dtype=torch.uint8, device=dev)
+    vc = torch.zeros_like(kc)
+    cu = d["cu_seqlens"].tolist()
+    for b, L in enumerate(lens):
+        kc[b, :, :L] = k8.view(torch.uint8)[cu[b]:cu[b + 1]].transpose(0, 1)
+        vc[b, :, :L] = v8.view(torch.uint8)[cu[b]:cu[b + 1]].transpose(0, 1)
+    outd = fk.flash_decode_gqa_hf_fp8(q, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), sl, None, sk, sv,
+                                      torch.float16, s_aux=d["s_aux"])
+    assert torch.equal(outd, outp)

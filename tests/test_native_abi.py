@@ -46,9 +46,10 @@ def test_invalid_arguments_are_rejected_without_touching_the_device():
     rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 32, 8, 64, 16, 0,
                                       0, 0, 0, 0, 0, 0, 0, 0, fake, 0, None)
     assert rc == 2 and "head_dim" in N.last_error()
-    rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 96, 8, 128, 16, 0,
+    rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 36, 8, 128, 16, 0,
                                       0, 0, 0, 0, 0, 0, 0, 0, fake, 0, None)
-    assert rc == 2 and "group size" in N.last_error()
+    assert rc == 1 and "multiple" in N.last_error()
+    assert L.fk_decode_workspace_bytes_gqa(0, 4, 36, 8, 0) == 0 and "bad sizes" in N.last_error()
     rc = L.fk_paged_flash_decode(fake, fake, fake, fake, fake, None, fake, 1, 32, 8, 128, 10, 32, 4, 0, 0, 0,
                                  None, None, None, *([0] * 11), fake, 0, None)
     assert rc in (1, 2)
