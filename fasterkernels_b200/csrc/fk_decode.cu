@@ -52,7 +52,7 @@
 
 namespace fk {
 
-constexpr int HEAD_DIM = 128;
+constexpr int HEAD_DIM = 128;  // largest head dim; workspace records, epilogue slots and Q rows are sized for it
 constexpr int GPAD = 8;        // MMA N: query heads of one KV group, padded
 constexpr int TILE = 64;       // tokens per pipeline stage
 constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
@@ -70,20 +70,21 @@ constexpr float NEG_INF = -__builtin_huge_valf();
 enum Layout { VARLEN = 0, DENSE = 1, PAGED = 2 };
 enum Flags { F_FIRST = 1, F_LAST = 2, F_WHOLE = 4, F_END = 8 };
 
-template <int KV>
+// Per KV element type and head dim D (128; 64 for 16-bit KV).
+template <int KV, int D>
 struct KvCfg {
   static constexpr bool FP8 = (KV == FK_DTYPE_E4M3);
   static constexpr bool BF16 = (KV == FK_DTYPE_BF16);
+  static_assert(D == 128 || (D == 64 && !FP8), "head dim 128, or 64 with 16-bit KV");
   static constexpr int ES = FP8 ? 1 : 2;                     // bytes per element
-  static constexpr int TILE_BYTES = TILE * HEAD_DIM * ES;    // K (or V) bytes per stage
-  static constexpr int PAGE_BYTES = PAGE * HEAD_DIM * ES;    // one page of K (or V)
+  static constexpr int NH = D * ES / 128;                    // 128-byte halves per row
+  static constexpr int KD = D / 16;                          // MMA k-steps (QK) / dim tiles (PV)
+  static constexpr int TILE_BYTES = TILE * D * ES;           // K (or V) bytes per stage
+  static constexpr int PAGE_BYTES = PAGE * D * ES;           // one page of K (or V)
   static constexpr int STAGES = FP8 ? 4 : 5;
   static constexpr int NSLOT = FP8 ? 1 : 2;                  // epilogue slots (smem budget: 2 CTAs/SM for FP8)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  static constexpr int BOX_D = FP8 ? 128 : 64;               // dims per TMA box (128 bytes)
-  static constexpr int NHALF = HEAD_DIM / BOX_D;             // boxes per 128-dim row
-  static constexpr int HALF_BYTES = TILE * 128;              // one [64 rows][128 B] box region
-  static constexpr int MINB = FP8 ? 2 : 1;                   // resident CTAs per SM
+  static constexpr int MINB = FP8 ? 2 : 1;                   // resident CTAs per SM (at least)
 };
 
 // One epilogue slot: the four consumer warps' online-softmax states of a
@@ -96,28 +97,22 @@ struct EpiSlot {
 
 // Shared-memory tile layouts of one K (or V) stage: TT = 64/HP tokens of each
 // of the item's HP KV heads, 128-byte swizzled (16-byte chunk index XOR
-// row & 7).  A 16-bit row is 256 bytes, stored as two 64-dim halves.
-//   16-bit VARLEN / DENSE: [head][half][TT rows][64 dims]   one TMA box per stage
-//   16-bit PAGED:          [page][head][half][16][64 dims]  one TMA box per page
-//   e4m3 VARLEN / DENSE:   [head][TT rows][128 dims]
-//   e4m3 PAGED:            [page][head][16][128 dims]
+// row & 7).  A row of D elements is NH = D * ES / 128 halves of 128 bytes
+// (16-bit D = 128: two 64-dim halves; 16-bit D = 64 and e4m3 D = 128: one).
+//   VARLEN / DENSE: [head][half][TT rows][128 B]   one TMA box per stage
+//   PAGED:          [page][head][half][16][128 B]  one TMA box per page
 // Row r of head hh, 16-byte chunk c is at row_off(hh, r) + (c >> 3) *
-// HALF_STRIDE + (((c & 7) ^ (r & 7)) << 4) (e4m3: c < 8).  All bases are
-// multiples of 1024 bytes, so the swizzle line of row r is r & 7 everywhere.
-template <int KV, int LAYOUT, int HP>
+// HALF_STRIDE + (((c & 7) ^ (r & 7)) << 4).  All bases are multiples of 1024
+// bytes, so the swizzle line of row r is r & 7 everywhere.
+template <int KV, int LAYOUT, int HP, int D>
 struct TileLayout {
-  static constexpr bool FP8 = KV == FK_DTYPE_E4M3;
   static constexpr bool PG = LAYOUT == 2;  // PAGED
+  static constexpr int NH = KvCfg<KV, D>::NH;
   static constexpr int TT = TILE / HP;
   static constexpr uint32_t HALF_STRIDE = PG ? 2048u : uint32_t(TT * 128);
   __device__ static __forceinline__ uint32_t row_off(int hh, int r) {
-    if constexpr (FP8) {
-      if constexpr (PG) return uint32_t((r >> 4) * (HP * 2048) + hh * 2048 + (r & 15) * 128);
-      else return uint32_t(hh * (TT * 128) + r * 128);
-    } else {
-      if constexpr (PG) return uint32_t((r >> 4) * (HP * 4096) + hh * 4096 + (r & 15) * 128);
-      else return uint32_t(hh * (2 * TT * 128) + r * 128);
-    }
+    if constexpr (PG) return uint32_t((r >> 4) * (HP * NH * 2048) + hh * (NH * 2048) + (r & 15) * 128);
+    else return uint32_t(hh * (NH * TT * 128) + r * 128);
   }
 };
 
@@ -185,6 +180,7 @@ struct Params {
   int num_ctas;
   int q_al16;  // q base and strides 16-byte aligned (rows can be copied with cp.async)
   int qc;      // query chunks of at most 8 heads per KV head: ceil(G / 8)
+  int head_dim;  // D (the kernel is instantiated per D; kept for host checks)
 };
 
 // Work items of a sequence and their two head slots hh < HP (an MMA N of 8
@@ -326,10 +322,11 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // ------------------------------------------------------------------------
 // Split pass.
 // ------------------------------------------------------------------------
-template <int KV, int LAYOUT, int HP>
-__global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
-  using C = KvCfg<KV>;
-  using TL = TileLayout<KV, LAYOUT, HP>;
+template <int KV, int LAYOUT, int HP, int D>
+__global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
+  using C = KvCfg<KV, D>;
+  using TL = TileLayout<KV, LAYOUT, HP, D>;
+  constexpr int KD = C::KD;
   constexpr int TT = TILE / HP;          // tokens per KV head in one stage
   constexpr int WPH = CWARPS / HP;       // consumer warps per KV head
   constexpr int PPT = TT / PAGE;         // pages per KV head in one stage
@@ -337,6 +334,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* stages = smem;
+  static_assert(D <= HEAD_DIM, "head dim");
   EpiSlot* eslot = reinterpret_cast<EpiSlot*>(smem + C::STAGES * C::STAGE_BYTES);  // [NSLOT]
   Meta* emeta = reinterpret_cast<Meta*>(eslot + C::NSLOT);                         // [NSLOT]
   Meta* meta = emeta + C::NSLOT;                                                   // [STAGES]
@@ -478,7 +476,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         const int idx = lane + 32 * k;
         const int hh = idx / (GPAD * 64), j = (idx >> 6) & (GPAD - 1), d = (idx & 63) * 2;
         const int qh = item_q<HP>(p, ih, hh, j);
-        qpre[k] = (j < item_g<HP>(p, ih, hh)) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d) : 0u;
+        qpre[k] = (j < item_g<HP>(p, ih, hh) && d < D) ? load_q_pair_raw(p, qb0 + static_cast<long long>(qh) * p.q_sh + d)
+                                                       : 0u;
       }
       qpre_b = bb;
       qpre_h = ih;
@@ -589,12 +588,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           if (tt == tbeg) {
             uint32_t* qs = qstage + stage * QWORDS;
             if (q_async) {
-              // the item's HP*G rows of 256 bytes, 16 bytes per copy
+              // the item's query rows of D * 2 bytes, 16 bytes per copy, into
+              // 256-byte row slots
               const uint32_t qd = smem_u32(qs);
               const long long qb0 = static_cast<long long>(b) * p.q_sb;
               const int g0 = item_g<HP>(p, hi, 0), g1 = HP == 2 ? item_g<HP>(p, hi, 1) : 0;
-              for (int u = lane; u < (g0 + g1) * 16; u += 32) {
-                const int r = u >> 4, c = u & 15;
+              for (int u = lane; u < (g0 + g1) * (D / 8); u += 32) {
+                const int r = u / (D / 8), c = u % (D / 8);
                 const int hh = r < g0 ? 0 : 1, j = r < g0 ? r : r - g0;
                 const int qh = item_q<HP>(p, hi, hh, j);
                 cp_async16(qd + (hh * GPAD + j) * 256 + c * 16,
@@ -635,7 +635,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           if constexpr (LAYOUT == PAGED) {
             if (phys >= 0) {
               // one box per page: 16 tokens x HP heads x 128 dims
-              const uint32_t off = lane * (HP * PAGE * 128 * C::ES);
+              const uint32_t off = lane * (HP * C::PAGE_BYTES);
               if constexpr (C::FP8) {
                 tma_load_4d(sK + off, &p.tk, fb, 0, 0, hcoord, phys);
                 tma_load_4d(sV + off, &p.tv, fb, 0, 0, hcoord, phys);
@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       long long t0;
       if (seq_len<LAYOUT>(p, b, &t0) == 0) {
         for (int qh = 0; qh < p.q_heads; ++qh)
-          for (int d = et; d < HEAD_DIM; d += ETHREADS)
+          for (int d = et; d < D; d += ETHREADS)
             store_out(p, static_cast<long long>(b) * p.o_sb + static_cast<long long>(qh) * p.o_sh + d, 0.f);
       }
     }
@@ -751,7 +751,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       const long long item = static_cast<long long>(mt.b) * KVI + mt.h;
       const long long obase = static_cast<long long>(mt.b) * p.o_sb;
       // One unit per thread and round: query head hd of KV head hh (head
-      // slot u / 8), dims (u % 8) * 4 + 32 k, k < 4 (a quarter warp reads
+      // slot u / 8), dims (u % 8) * 4 + 32 k, k < D / 32 (a quarter warp reads
       // 128 contiguous bytes of the slot: no bank conflicts).
       const int g0 = item_g<HP>(p, mt.h, 0), g1 = HP == 2 ? item_g<HP>(p, mt.h, 1) : 0;
       for (int u = et; u < (g0 + g1) * 8; u += ETHREADS) {
@@ -768,11 +768,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         }
         float4 A[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < D / 32; ++k) A[k] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int w = 0; w < WPH; ++w) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
+          for (int k = 0; k < D / 32; ++k) {
             const float4 v = *reinterpret_cast<const float4*>(&E.cacc[hh * WPH + w][hd][d4 + 32 * k]);
             A[k].x += ew[w] * v.x;
             A[k].y += ew[w] * v.y;
@@ -787,7 +787,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
           sink_norm(L, M, p.s_aux, qh, &e, &Lf);
           const long long ob = obase + static_cast<long long>(qh) * p.o_sh + d4;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
+          for (int k = 0; k < D / 32; ++k) {
             store_out(p, ob + 32 * k + 0, norm_out(A[k].x, e, Lf, sv));
             store_out(p, ob + 32 * k + 1, norm_out(A[k].y, e, Lf, sv));
             store_out(p, ob + 32 * k + 2, norm_out(A[k].z, e, Lf, sv));
@@ -796,7 +796,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         } else {
           float4* dst = reinterpret_cast<float4*>(&ws_acc[(static_cast<long long>(mt.seg) * GMAX + hs) * HEAD_DIM + d4]);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) dst[8 * k] = A[k];
+          for (int k = 0; k < D / 32; ++k) dst[8 * k] = A[k];
           if ((u & 7) == 0) ws_ml[static_cast<long long>(mt.seg) * GMAX + hs] = make_float2(M, L);
         }
       }
@@ -816,10 +816,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       named_bar_sync(2, ETHREADS);
       if (!s_last) continue;
       __threadfence();
-      // All head slots in parallel: unit u = (slot u / 8, dims (u % 8) * 16 ..
-      // +16); each thread merges its units with 4 segments' loads in flight.
-      for (int u = et; u < (g0 + g1) * 8; u += ETHREADS) {
-        const int r = u >> 3, d0 = (u & 7) * 16;
+      // All head slots in parallel: unit u = (slot u / KD, dims (u % KD) * 16
+      // .. +16); each thread merges its units with 4 segments' loads in flight.
+      for (int u = et; u < (g0 + g1) * KD; u += ETHREADS) {
+        const int r = u / KD, d0 = (u % KD) * 16;
         const int hh = r < g0 ? 0 : 1, hd = r < g0 ? r : r - g0;
         const int hs = hh * GPAD + hd;
         float M = NEG_INF, L = 0.f;
@@ -884,10 +884,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
   const int hk = chunk_pairs<HP>(p) ? 0 : hh;  // its KV head's tile in the stage
   const int r0 = (warp % WPH) * 16;      // its 16 rows of that head's tile
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
-  const float qk_scale = rsqrtf(static_cast<float>(HEAD_DIM)) * LOG2E * sk;
+  const float qk_scale = rsqrtf(static_cast<float>(D)) * LOG2E * sk;
 
-  float m[2], l[2], acc[8][4];
-  uint32_t qb[8][2];
+  float m[2], l[2], acc[KD][4];
+  uint32_t qb[KD][2];
   int stage = 0;
   uint32_t phase = 0;
   int eb = 0;            // epilogue slot
@@ -934,12 +934,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       m[0] = m[1] = NEG_INF;
       l[0] = l[1] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      for (int i = 0; i < KD; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
       // the producer staged this item's Q rows (MMA type, zero-padded to 8
       // heads) next to the segment's first tile
       const uint32_t* qrow = qstage + stage * QWORDS + hh * (GPAD * 64) + g * 64;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < KD; ++j) {
         int d0, d1;
         if constexpr (FP8) {
           d0 = (j < 4) ? (16 * t + 4 * j) : (64 + 16 * t + 4 * (j - 4));
@@ -989,7 +989,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         const uint32_t kb = sK + TL::row_off(hk, krow);
         const int ksw = krow & 7;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < KD; ++j) {
           const int c = ((j & 3) << 1) + (lq >> 1);
           uint32_t a0, a1, a2, a3;
           ldsm_x4(kb + (j >> 2) * TL::HALF_STRIDE + ((c ^ ksw) << 4), a0, a1, a2, a3);
@@ -1023,7 +1023,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
       m[0] = mn0;
       m[1] = mn1;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < KD; ++i) {
         acc[i][0] *= al0;
         acc[i][1] *= al1;
         acc[i][2] *= al0;
@@ -1047,7 +1047,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         const uint32_t w2[4] = {x[2].x, x[2].y, x[2].z, x[2].w};
         const uint32_t w3[4] = {x[3].x, x[3].y, x[3].z, x[3].w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < KD; ++i) {
           const uint32_t sel = (i & 1) ? 0x7362u : 0x5140u;
           const uint32_t u01 = __byte_perm(w0[i >> 1], w1[i >> 1], sel);
           const uint32_t u89 = __byte_perm(w2[i >> 1], w3[i >> 1], sel);
@@ -1064,7 +1064,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         const uint32_t vb = sV + TL::row_off(hk, vrow);
         const int vsw = vrow & 7;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < KD; ++i) {
           const int c = ((2 * i) & 7) + (lq & 1);
           uint32_t a0, a1, a2, a3;
           ldsm_x4_t(vb + (i >> 2) * TL::HALF_STRIDE + ((c ^ vsw) << 4), a0, a1, a2, a3);
@@ -1101,7 +1101,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV>::MINB) decode_split_kernel(
         E.cl[warp][2 * t + 1] = l[1];
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < KD; ++i) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const int d = FP8 ? (16 * cg + 2 * i + r) : (16 * i + g + 8 * r);
@@ -1177,9 +1177,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-template <int KV, int HP>
+template <int KV, int HP, int D>
 constexpr size_t smem_bytes() {
-  using C = KvCfg<KV>;
+  using C = KvCfg<KV, D>;
   return 1024 + C::STAGES * (C::STAGE_BYTES + sizeof(Meta) + sizeof(uint32_t) * HP * GPAD * 64 + 2 * sizeof(uint64_t)) +
          C::NSLOT * (sizeof(EpiSlot) + sizeof(Meta) + 2 * sizeof(uint64_t));
 }
@@ -1212,57 +1212,73 @@ inline uint32_t box_heads(int kv_heads, int qc) {
   return static_cast<uint32_t>((qc > 1) ? 1 : hp);
 }
 
-template <int KV, int LAYOUT, int HP>
+template <int KV, int LAYOUT, int HP, int D>
 int prepare_kernel(int device) {
   static bool done[64] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lk(mu);
   if (device < 0 || device >= 64) return fail(FK_ERR_INVALID_ARG, "device index %d out of range", device);
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP>,
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP, D>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_bytes<KV, HP>()));
+                                         static_cast<int>(smem_bytes<KV, HP, D>()));
     if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done[device] = true;
   }
   return FK_OK;
 }
 
-template <int KV, int HP>
+template <int KV, int HP, int D>
 int occupancy(int device, int* per_sm) {
-  int rc = prepare_kernel<KV, VARLEN, HP>(device);
+  int rc = prepare_kernel<KV, VARLEN, HP, D>(device);
   if (rc != FK_OK) return rc;
-  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, decode_split_kernel<KV, VARLEN, HP>,
-                                                                      THREADS, smem_bytes<KV, HP>());
+  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, decode_split_kernel<KV, VARLEN, HP, D>,
+                                                                      THREADS, smem_bytes<KV, HP, D>());
   return e == cudaSuccess ? FK_OK : fail(FK_ERR_CUDA, "occupancy query failed: %s", cudaGetErrorString(e));
 }
 
-// Resident CTAs of the decode kernel on `device` for KV type `kv` and HP KV
-// heads per item: the persistent grid size S.  It does not depend on the
-// layout (the layout instantiations share shared-memory footprint and launch
-// bounds), so paged, dense and varlen calls plan identical segments.
-int num_work_ctas(int device, int kv, int hp) {
-  static int cache[64][3][2] = {};
+// Resident CTAs of the decode kernel on `device` for KV type `kv`, HP KV
+// heads per item and head dim d: the persistent grid size S.  It does not
+// depend on the layout (the layout instantiations share shared-memory
+// footprint and launch bounds), so paged, dense and varlen calls plan
+// identical segments.
+int num_work_ctas(int device, int kv, int hp, int d = HEAD_DIM) {
+  static int cache[64][3][2][2] = {};
   static std::mutex mu;
   if (device < 0 || device >= 64 || kv < 0 || kv > 2 || hp < 1 || hp > 2) return 0;
+  if (d != 128 && (d != 64 || kv == FK_DTYPE_E4M3)) return 0;
+  const int di = d == 64 ? 0 : 1;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (cache[device][kv][hp - 1] > 0) return cache[device][kv][hp - 1];
+    if (cache[device][kv][hp - 1][di] > 0) return cache[device][kv][hp - 1][di];
   }
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
   int per_sm = 0, prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
+#define FK_OCC(KVT, H, DD) occupancy<KVT, H, DD>(device, &per_sm)
+#define FK_OCC16(KVT) \
+  (d == 64 ? (hp == 2 ? FK_OCC(KVT, 2, 64) : FK_OCC(KVT, 1, 64)) : (hp == 2 ? FK_OCC(KVT, 2, 128) : FK_OCC(KVT, 1, 128)))
   int rc;
-  if (kv == FK_DTYPE_F16) rc = hp == 2 ? occupancy<FK_DTYPE_F16, 2>(device, &per_sm) : occupancy<FK_DTYPE_F16, 1>(device, &per_sm);
-  else if (kv == FK_DTYPE_BF16) rc = hp == 2 ? occupancy<FK_DTYPE_BF16, 2>(device, &per_sm) : occupancy<FK_DTYPE_BF16, 1>(device, &per_sm);
-  else rc = hp == 2 ? occupancy<FK_DTYPE_E4M3, 2>(device, &per_sm) : occupancy<FK_DTYPE_E4M3, 1>(device, &per_sm);
+  if (kv == FK_DTYPE_F16) rc = FK_OCC16(FK_DTYPE_F16);
+  else if (kv == FK_DTYPE_BF16) rc = FK_OCC16(FK_DTYPE_BF16);
+  else rc = hp == 2 ? FK_OCC(FK_DTYPE_E4M3, 2, 128) : FK_OCC(FK_DTYPE_E4M3, 1, 128);
+#undef FK_OCC16
+#undef FK_OCC
   if (prev != device) cudaSetDevice(prev);
   if (rc != FK_OK || per_sm <= 0) return 0;
   std::lock_guard<std::mutex> lk(mu);
-  cache[device][kv][hp - 1] = sms * per_sm;
-  return cache[device][kv][hp - 1];
+  cache[device][kv][hp - 1][di] = sms * per_sm;
+  return cache[device][kv][hp - 1][di];
+}
+
+// Grid size a workspace must be planned for: the largest over the head dims
+// the KV type supports (the workspace size functions do not take the head dim).
+int num_work_ctas_any_d(int device, int kv, int hp) {
+  const int s128 = num_work_ctas(device, kv, hp, 128);
+  const int s64 = (kv == FK_DTYPE_E4M3) ? 0 : num_work_ctas(device, kv, hp, 64);
+  return (s128 <= 0 || (kv != FK_DTYPE_E4M3 && s64 <= 0)) ? 0 : (s128 > s64 ? s128 : s64);
 }
 
 int encode_map(CUtensorMap* map, int kv, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_b,
@@ -1297,7 +1313,8 @@ int common_checks(const void* q, const void* k, const void* v, const void* out, 
   if (ws == nullptr) return fail(FK_ERR_WORKSPACE, "workspace must be non-null");
   if (batch < 0 || q_heads <= 0 || kv_heads <= 0)
     return fail(FK_ERR_INVALID_ARG, "bad sizes: batch=%d q_heads=%d kv_heads=%d", batch, q_heads, kv_heads);
-  if (head_dim != HEAD_DIM) return fail(FK_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (head_dim != 128 && !(head_dim == 64 && kv_dtype != FK_DTYPE_E4M3))
+    return fail(FK_ERR_UNSUPPORTED, "head_dim must be 128, or 64 with f16/bf16 KV (got %d)", head_dim);
   if (q_heads % kv_heads != 0)
     return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a multiple of kv_heads (%d)", q_heads, kv_heads);
   if (!is16(out_dtype)) return fail(FK_ERR_UNSUPPORTED, "out dtype must be f16 or bf16");
@@ -1352,14 +1369,14 @@ bool pdl_safe(const Params& p, cudaStream_t stream) {
   const size_t q_es = (p.q_dtype == FK_DTYPE_E4M3) ? 1 : 2;
   const long long qh = static_cast<long long>(p.q_heads) - 1, b = static_cast<long long>(p.B) - 1;
   const ByteRange in[7] = {
-      span(p.q, b * p.q_sb + qh * p.q_sh + HEAD_DIM - 1, q_es),
+      span(p.q, b * p.q_sb + qh * p.q_sh + p.head_dim - 1, q_es),
       span(p.lens, p.B, 4),
       span(p.starts, b, 4),
       span(p.bt, b * p.bt_sb + p.max_blocks - 1, 4),
       span(p.scale_q, 0, 4),
       span(p.scale_k, 0, 4),
       span(p.s_aux, qh, 4)};
-  const ByteRange out = span(p.out, b * p.o_sb + qh * p.o_sh + HEAD_DIM - 1, 2);
+  const ByteRange out = span(p.out, b * p.o_sb + qh * p.o_sh + p.head_dim - 1, 2);
   std::lock_guard<std::mutex> lk(g_last_out_mu);
   auto it = g_last_out.find(stream);
   bool safe = true;
@@ -1370,21 +1387,21 @@ bool pdl_safe(const Params& p, cudaStream_t stream) {
   return safe;
 }
 
-template <int KV, int LAYOUT, int HP>
+template <int KV, int LAYOUT, int HP, int D>
 int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
-  const int rc = prepare_kernel<KV, LAYOUT, HP>(device);
+  const int rc = prepare_kernel<KV, LAYOUT, HP, D>(device);
   if (rc != FK_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S);
   cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = smem_bytes<KV, HP>();
+  cfg.dynamicSmemBytes = smem_bytes<KV, HP, D>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = (pdl_enabled() && pdl_safe(p, stream)) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP, D>, p);
   if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaLaunchKernelEx: %s", cudaGetErrorString(e));
   return FK_OK;
 }
@@ -1392,7 +1409,7 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
 template <int LAYOUT>
 int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) {
   const int hp = hp_for(p.kv_heads, p.qc);
-  const int S = num_work_ctas(device, kv, hp);
+  const int S = num_work_ctas(device, kv, hp, p.head_dim);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   p.num_ctas = S;
   const int kvq = p.kv_heads * p.qc;  // (KV head, query chunk) pairs per sequence
@@ -1408,13 +1425,15 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
   prof_mark(0, stream);
+#define FK_L(KVT, H, DD) launch_one<KVT, LAYOUT, H, DD>(p, S, device, stream)
+#define FK_L16(KVT) \
+  (p.head_dim == 64 ? (hp == 2 ? FK_L(KVT, 2, 64) : FK_L(KVT, 1, 64)) : (hp == 2 ? FK_L(KVT, 2, 128) : FK_L(KVT, 1, 128)))
   int rc;
-  if (kv == FK_DTYPE_F16)
-    rc = hp == 2 ? launch_one<FK_DTYPE_F16, LAYOUT, 2>(p, S, device, stream) : launch_one<FK_DTYPE_F16, LAYOUT, 1>(p, S, device, stream);
-  else if (kv == FK_DTYPE_BF16)
-    rc = hp == 2 ? launch_one<FK_DTYPE_BF16, LAYOUT, 2>(p, S, device, stream) : launch_one<FK_DTYPE_BF16, LAYOUT, 1>(p, S, device, stream);
-  else
-    rc = hp == 2 ? launch_one<FK_DTYPE_E4M3, LAYOUT, 2>(p, S, device, stream) : launch_one<FK_DTYPE_E4M3, LAYOUT, 1>(p, S, device, stream);
+  if (kv == FK_DTYPE_F16) rc = FK_L16(FK_DTYPE_F16);
+  else if (kv == FK_DTYPE_BF16) rc = FK_L16(FK_DTYPE_BF16);
+  else rc = hp == 2 ? FK_L(FK_DTYPE_E4M3, 2, 128) : FK_L(FK_DTYPE_E4M3, 1, 128);
+#undef FK_L16
+#undef FK_L
   if (rc == FK_OK) {
     prof_mark(1, stream);
     const cudaError_t e = cudaGetLastError();
@@ -1433,9 +1452,10 @@ int check_q_align(const void* q, int q_dtype, int64_t sq_b, int64_t sq_h) {
 }
 
 void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out, int64_t so_b, int64_t so_h,
-                 const float* s_aux, int batch, int q_heads, int kv_heads, int q_dtype, int out_dtype,
+                 const float* s_aux, int batch, int q_heads, int kv_heads, int head_dim, int q_dtype, int out_dtype,
                  const float* scale_q, const float* scale_k, const float* scale_v, void* ws) {
   p.q = q;
+  p.head_dim = head_dim;
   p.q_sb = sq_b;
   p.q_sh = sq_h;
   p.out = out;
@@ -1476,7 +1496,7 @@ extern "C" size_t fk_decode_workspace_bytes_gqa(int device, int batch, int q_hea
     return 0;
   }
   const int qc = qc_for(q_heads, kv_heads);
-  const int S = num_work_ctas(device, kv_dtype, hp_for(kv_heads, qc));
+  const int S = num_work_ctas_any_d(device, kv_dtype, hp_for(kv_heads, qc));
   if (S <= 0) {
     fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
     return 0;
@@ -1507,16 +1527,17 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
     return fail(FK_ERR_INVALID_ARG, "k/v strides must be multiples of 16 bytes");
   Params p;
   memset(&p, 0, sizeof(p));
-  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, dtype, dtype, nullptr, nullptr,
+  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, head_dim, dtype, dtype, nullptr, nullptr,
               nullptr, workspace);
   p.lens = cu_seqlens_k;
   const uint64_t T = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
   const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
   const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
-  // 16-bit rows as (64 dims, T rows, 2 halves [128 B apart], heads): one box
-  // {64, 64/hp, 2, hp} per stage lands as [head][half][rows][64].
-  const uint64_t dims[4] = {64, T, 2, static_cast<uint64_t>(kv_heads)};
-  const uint32_t box[4] = {64, TILE / hp, 2, hb};
+  // 16-bit rows as (64 dims, T rows, D/64 halves [128 B apart], heads): one
+  // box {64, 64/hp, D/64, hp} per stage lands as [head][half][rows][64].
+  const uint32_t nh = static_cast<uint32_t>(head_dim / 64);
+  const uint64_t dims[4] = {64, T, nh, static_cast<uint64_t>(kv_heads)};
+  const uint32_t box[4] = {64, TILE / hp, nh, hb};
   const uint64_t ks[3] = {static_cast<uint64_t>(sk_t) * 2, 128, static_cast<uint64_t>(sk_h) * 2};
   const uint64_t vs[3] = {static_cast<uint64_t>(sv_t) * 2, 128, static_cast<uint64_t>(sv_h) * 2};
   if ((rc = encode_map(&p.tk, dtype, 4, k_varlen, dims, ks, box)) != FK_OK) return rc;
@@ -1546,7 +1567,7 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
     return fail(FK_ERR_INVALID_ARG, "k/v cache strides must be multiples of 16 bytes");
   Params p;
   memset(&p, 0, sizeof(p));
-  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, q_dtype, out_dtype, scale_q,
+  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, head_dim, q_dtype, out_dtype, scale_q,
               scale_k, scale_v, workspace);
   p.lens = cache_lens;
   p.starts = start_k_offsets;
@@ -1563,9 +1584,11 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
     if ((rc = encode_map(&p.tk, kv_dtype, 4, k_cache, dims, ks, box)) != FK_OK) return rc;
     if ((rc = encode_map(&p.tv, kv_dtype, 4, v_cache, dims, vs, box)) != FK_OK) return rc;
   } else {
-    // (64 dims, S rows, 2 halves, heads, batch): box {64, 64/hp, 2, hp, 1} -> [head][half][rows][64]
-    const uint64_t dims[5] = {64, static_cast<uint64_t>(max_seqlen), 2, static_cast<uint64_t>(kv_heads), Bd};
-    const uint32_t box[5] = {64, TILE / hp, 2, hb, 1};
+    // (64 dims, S rows, D/64 halves, heads, batch): box {64, 64/hp, D/64, hp, 1}
+    // -> [head][half][rows][64]
+    const uint32_t nh = static_cast<uint32_t>(head_dim / 64);
+    const uint64_t dims[5] = {64, static_cast<uint64_t>(max_seqlen), nh, static_cast<uint64_t>(kv_heads), Bd};
+    const uint32_t box[5] = {64, TILE / hp, nh, hb, 1};
     const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
                             static_cast<uint64_t>(sk_b) * 2};
     const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
@@ -1602,7 +1625,7 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   if (num_pages > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "num_pages too large");
   Params p;
   memset(&p, 0, sizeof(p));
-  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, q_dtype, out_dtype, scale_q,
+  fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, head_dim, q_dtype, out_dtype, scale_q,
               scale_k, scale_v, workspace);
   p.lens = seq_lens;
   p.bt = block_table;
@@ -1620,11 +1643,12 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
     if ((rc = encode_map(&p.tk, kv_dtype, 4, k_pool, dims, ks, box)) != FK_OK) return rc;
     if ((rc = encode_map(&p.tv, kv_dtype, 4, v_pool, dims, vs, box)) != FK_OK) return rc;
   } else {
-    // 16-bit: the head dim is split into (64 dims, 2 halves); the half index is
-    // the third dimension (stride 128 B), so one box {64, 16, 2, hp} carries a
-    // page for the item's heads and lands as [head][half][16 rows][64 dims].
-    const uint64_t dims[5] = {64, PAGE, 2, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
-    const uint32_t box[5] = {64, PAGE, 2, hb, 1};
+    // 16-bit: the head dim is split into (64 dims, D/64 halves); the half index
+    // is the third dimension (stride 128 B), so one box {64, 16, D/64, hp}
+    // carries a page for the item's heads and lands as [head][half][16][64].
+    const uint32_t nh = static_cast<uint32_t>(head_dim / 64);
+    const uint64_t dims[5] = {64, PAGE, nh, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};
+    const uint32_t box[5] = {64, PAGE, nh, hb, 1};
     const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
                             static_cast<uint64_t>(sk_p) * 2};
     const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
@@ -1738,7 +1762,7 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
   if (q_heads <= 0 || q_heads % kv_heads != 0)
     return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a positive multiple of kv_heads (%d)", q_heads, kv_heads);
   const int qc = qc_for(q_heads, kv_heads);
-  const int S = num_work_ctas(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp_for(kv_heads, qc));
+  const int S = num_work_ctas_any_d(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp_for(kv_heads, qc));
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   const size_t need = WsLayout::min_bytes(batch, kv_heads * qc, S);
   if (need > NOALLOC_SCRATCH_BYTES)

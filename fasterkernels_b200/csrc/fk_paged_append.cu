@@ -23,7 +23,7 @@ int fail(int code, const char* fmt, ...);
 struct AppendParams {
   const void* k_new;
   const void* v_new;
-  long long kn_b, kn_h, vn_b, vn_h;  // element strides of k_new / v_new [B, KVH, 128]
+  long long kn_b, kn_h, vn_b, vn_h;  // element strides of k_new / v_new [B, KVH, D]
   void* k_pool;
   void* v_pool;
   long long kp_p, kp_h, kp_s, vp_p, vp_h, vp_s;  // element strides of the pools
@@ -37,6 +37,7 @@ struct AppendParams {
   const float* scale_v;
   int* status;        // optional FK_STATUS_* word
   int B, kvh, in_dtype, pool_dtype;
+  int head_dim;       // 128, or 64
 };
 
 __device__ __forceinline__ float load_elem(const void* base, long long i, int dt) {
@@ -44,8 +45,9 @@ __device__ __forceinline__ float load_elem(const void* base, long long i, int dt
   return __half2float(static_cast<const __half*>(base)[i]);
 }
 
-// One CTA per sequence; thread t handles dims 8*(t%16) .. +7 of KV head t/16
-// (and further heads in steps of blockDim/16).
+// One CTA per sequence; with tph = D / 8 threads per head, thread t handles
+// dims 8*(t%tph) .. +7 of KV head t/tph (and further heads in steps of
+// blockDim/tph).
 __global__ void __launch_bounds__(128) paged_append_kernel(const AppendParams p) {
   const int b = blockIdx.x;
   const int pos = p.pos[b];
@@ -60,8 +62,9 @@ __global__ void __launch_bounds__(128) paged_append_kernel(const AppendParams p)
   // division: multiplying by a reciprocal would round differently)
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
   const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
-  const int d0 = (threadIdx.x & 15) * 8;
-  for (int h = threadIdx.x >> 4; h < p.kvh; h += blockDim.x >> 4) {
+  const int tph = p.head_dim / 8;
+  const int d0 = (threadIdx.x % tph) * 8;
+  for (int h = threadIdx.x / tph; h < p.kvh; h += blockDim.x / tph) {
     const long long ki = static_cast<long long>(b) * p.kn_b + static_cast<long long>(h) * p.kn_h + d0;
     const long long vi = static_cast<long long>(b) * p.vn_b + static_cast<long long>(h) * p.vn_h + d0;
     const long long ko = static_cast<long long>(phys) * p.kp_p + static_cast<long long>(h) * p.kp_h +
@@ -115,7 +118,7 @@ extern "C" int fk_paged_kv_append(const void* k_new, const void* v_new, int in_d
     return fail(FK_ERR_INVALID_ARG, "k_new, v_new, pools, block_table and positions must be non-null");
   if (batch < 0 || kv_heads <= 0 || num_pages <= 0 || max_blocks < 0)
     return fail(FK_ERR_INVALID_ARG, "bad sizes");
-  if (head_dim != 128) return fail(FK_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", head_dim);
+  if (head_dim != 128 && head_dim != 64) return fail(FK_ERR_UNSUPPORTED, "head_dim must be 128 or 64 (got %d)", head_dim);
   if (in_dtype != FK_DTYPE_F16 && in_dtype != FK_DTYPE_BF16)
     return fail(FK_ERR_UNSUPPORTED, "new K/V must be f16 or bf16");
   if (pool_dtype != FK_DTYPE_E4M3 && pool_dtype != in_dtype)
@@ -154,6 +157,7 @@ extern "C" int fk_paged_kv_append(const void* k_new, const void* v_new, int in_d
   p.kvh = kv_heads;
   p.in_dtype = in_dtype;
   p.pool_dtype = pool_dtype;
+  p.head_dim = head_dim;
   paged_append_kernel<<<batch, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(FK_ERR_CUDA, "paged append launch failed: %s", cudaGetErrorString(e));

@@ -20,6 +20,7 @@ import torch
 from . import _native as N
 
 HEAD_DIM = 128
+HEAD_DIMS = (64, 128)  # 64 with float16/bfloat16 KV only
 
 
 def _inner_contig(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -52,8 +53,9 @@ def flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux=None, *, 
     """out[b, qh] = attention of q[b, qh] over k/v rows cu_seqlens_k[b]..cu_seqlens_k[b+1]-1
     of KV head qh // G, with the optional per-query-head sink logit s_aux[qh].
 
-    q [B, Q_H, 128], k_varlen / v_varlen [T, KV_H, 128] (float16 or bfloat16),
-    cu_seqlens_k [B+1] int32, s_aux [Q_H] float32 or None.  Returns [B, Q_H, 128].
+    q [B, Q_H, D], k_varlen / v_varlen [T, KV_H, D] (float16 or bfloat16,
+    D = 128 or 64), cu_seqlens_k [B+1] int32, s_aux [Q_H] float32 or None.
+    Returns [B, Q_H, D].
     """
     if q.dim() != 3 or k_varlen.dim() != 3 or v_varlen.dim() != 3:
         raise ValueError("q must be [B, Q_H, D] and k_varlen/v_varlen [T, KV_H, D]")
@@ -68,8 +70,8 @@ def flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux=None, *, 
         raise TypeError("flash_decode_gqa_varlen takes float16 or bfloat16 tensors")
     B, QH, D = q.shape
     T, KVH, D2 = k_varlen.shape
-    if D != HEAD_DIM or D2 != HEAD_DIM or v_varlen.shape != k_varlen.shape:
-        raise ValueError(f"head_dim must be {HEAD_DIM} and k/v shapes must match")
+    if D not in HEAD_DIMS or D2 != D or v_varlen.shape != k_varlen.shape:
+        raise ValueError(f"head_dim must be one of {HEAD_DIMS} and q/k/v head dims and k/v shapes must match")
     if cu_seqlens_k.numel() != B + 1:
         raise ValueError("cu_seqlens_k must have batch + 1 entries")
     q = _inner_contig(q, "q")
@@ -80,7 +82,7 @@ def flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux=None, *, 
     if out is None:
         out = torch.empty(B, QH, D, dtype=q.dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != q.dtype or out.stride(-1) != 1:
-        raise ValueError("out must be [B, Q_H, 128] of q's dtype with unit inner stride")
+        raise ValueError("out must be [B, Q_H, D] of q's dtype with unit inner stride")
     code = N.dtype_code(q.dtype)
     ws = N.workspace(dev, B, QH, KVH, code)
     rc = N.lib().fk_flash_decode_gqa_varlen(

@@ -21,7 +21,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _native as N
-from .gqa_decode import HEAD_DIM, _check_idx, _check_sink, _inner_contig
+from .gqa_decode import HEAD_DIMS, _check_idx, _check_sink, _inner_contig
 
 _DECODE_NUM_SPLITS: int = 1
 
@@ -65,8 +65,8 @@ def dense_decode(q, k_cache, v_cache, cache_lens, start_k_offsets=None, *, s_aux
         raise ValueError("k_cache and v_cache must match in shape and dtype")
     B, QH, D = q.shape
     Bk, KVH, S, D2 = k_cache.shape
-    if D != HEAD_DIM or D2 != HEAD_DIM:
-        raise ValueError(f"head_dim must be {HEAD_DIM}")
+    if D not in HEAD_DIMS or D2 != D or (D != 128 and k_cache.element_size() == 1):
+        raise ValueError(f"head_dim must be one of {HEAD_DIMS} (128 for an e4m3 cache) and match the cache")
     if Bk < B:
         raise ValueError("cache batch is smaller than q's batch")
     kv_code = N.dtype_code(k_cache.dtype)
@@ -88,7 +88,7 @@ def dense_decode(q, k_cache, v_cache, cache_lens, start_k_offsets=None, *, s_aux
     if out is None:
         out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
-        raise ValueError("out must be [B, Q_H, 128] of out_dtype with unit inner stride")
+        raise ValueError("out must be [B, Q_H, D] of out_dtype with unit inner stride")
     ws = N.workspace(dev, B, QH, KVH, kv_code)
     rc = N.lib().fk_flash_decode_gqa_hf_dense(
         N.ptr(q), N.ptr(k_cache), N.ptr(v_cache), N.ptr(lens), N.ptr(starts), N.ptr(s_aux), N.ptr(out),
@@ -167,7 +167,7 @@ def _fallback(module, query_states, key_states, value_states, attention_mask, sc
 
 
 def _is_decode(kwargs, query_states):
-    return (query_states.shape[2] == 1 and query_states.is_cuda and query_states.shape[-1] == HEAD_DIM
+    return (query_states.shape[2] == 1 and query_states.is_cuda and query_states.shape[-1] in HEAD_DIMS
             and (kwargs.get("past_key_values") is not None or kwargs.get("cache_position") is not None))
 
 

@@ -23,12 +23,13 @@ def paged_kv_append(k_new, v_new, k_pool, v_pool, block_table, positions, *, sca
     in place when ``increment``)."""
     if k_new.dim() == 4:
         k_new, v_new = k_new.squeeze(2), v_new.squeeze(2)
-    if k_new.dim() != 3 or k_new.shape != v_new.shape or k_new.shape[-1] != 128:
-        raise ValueError("k_new / v_new must be [B, KV_H, 128]")
+    if k_new.dim() != 3 or k_new.shape != v_new.shape or k_new.shape[-1] not in (64, 128):
+        raise ValueError("k_new / v_new must be [B, KV_H, D], D = 128 or 64")
     if not k_new.is_cuda:
         raise ValueError("paged_kv_append runs on CUDA tensors only")
-    if k_pool.dim() != 4 or k_pool.shape != v_pool.shape or k_pool.shape[2] != 16 or k_pool.shape[3] != 128:
-        raise ValueError("pools must be [num_pages, KV_H, 16, 128]")
+    if (k_pool.dim() != 4 or k_pool.shape != v_pool.shape or k_pool.shape[2] != 16
+            or k_pool.shape[3] != k_new.shape[-1]):
+        raise ValueError("pools must be [num_pages, KV_H, 16, D] with the head dim of k_new")
     B, KVH, D = k_new.shape
     if k_pool.shape[1] != KVH:
         raise ValueError("pool KV heads do not match k_new")

@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native as N
-from ..gqa_decode import HEAD_DIM, _check_idx, _check_sink, _inner_contig
+from ..gqa_decode import HEAD_DIMS, _check_idx, _check_sink, _inner_contig
 from ..gqa_decode_hf import _scale_ptr
 
 
@@ -33,8 +33,8 @@ def paged_flash_decode(q, k_pool, v_pool, block_table, seq_lens, page_size, *, s
     P, KVH, PS, D2 = k_pool.shape
     if int(page_size) != PS or PS != 16:
         raise ValueError(f"page_size must be 16 and match the pool (pool has {PS})")
-    if D != HEAD_DIM or D2 != HEAD_DIM:
-        raise ValueError(f"head_dim must be {HEAD_DIM}")
+    if D not in HEAD_DIMS or D2 != D or (D != 128 and k_pool.element_size() == 1):
+        raise ValueError(f"head_dim must be one of {HEAD_DIMS} (128 for an e4m3 pool) and match the pools")
     kv_code = N.dtype_code(k_pool.dtype)
     q_code = N.dtype_code(q.dtype)
     if kv_code != N.FK_DTYPE_E4M3 and q.dtype != k_pool.dtype:
@@ -62,7 +62,7 @@ def paged_flash_decode(q, k_pool, v_pool, block_table, seq_lens, page_size, *, s
     if out is None:
         out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
-        raise ValueError("out must be [B, Q_H, 128] of out_dtype with unit inner stride")
+        raise ValueError("out must be [B, Q_H, D] of out_dtype with unit inner stride")
     ws = N.workspace(dev, B, QH, KVH, kv_code)
     rc = N.lib().fk_paged_flash_decode(
         N.ptr(q), N.ptr(k_pool), N.ptr(v_pool), N.ptr(bt), N.ptr(lens), N.ptr(s_aux), N.ptr(out),

@@ -72,7 +72,7 @@ def _gen(device, seed):
     return g
 
 
-def make_varlen(lens, q_heads, kv_heads, dtype, device, seed=0, sinks=True):
+def make_varlen(lens, q_heads, kv_heads, dtype, device, seed=0, sinks=True, head_dim=D):
     """q [B,QH,D], k/v [T,KVH,D], cu_seqlens [B+1] int32, s_aux [QH] fp32 or None."""
     B = len(lens)
     g = _gen(device, seed + 1)
@@ -80,9 +80,9 @@ def make_varlen(lens, q_heads, kv_heads, dtype, device, seed=0, sinks=True):
     cu[1:] = torch.cumsum(torch.tensor(lens, dtype=torch.int64), 0).to(torch.int32)
     T = int(cu[-1])
     gd = torch.float32 if dtype in (torch.float32, torch.float8_e4m3fn) else dtype
-    q = torch.randn(B, q_heads, D, generator=g, device=device, dtype=gd)
-    k = torch.randn(T, kv_heads, D, generator=g, device=device, dtype=gd)
-    v = torch.randn(T, kv_heads, D, generator=g, device=device, dtype=gd)
+    q = torch.randn(B, q_heads, head_dim, generator=g, device=device, dtype=gd)
+    k = torch.randn(T, kv_heads, head_dim, generator=g, device=device, dtype=gd)
+    v = torch.randn(T, kv_heads, head_dim, generator=g, device=device, dtype=gd)
     s_aux = torch.randn(q_heads, generator=g, device=device, dtype=torch.float32) if sinks else None
     return dict(q=q, k=k, v=v, cu_seqlens=cu.to(device), s_aux=s_aux, lens=list(lens))
 
@@ -103,8 +103,8 @@ def varlen_to_paged(k, v, lens, pool_factor=1.25, seed=0, max_blocks=None):
     for b in range(B):
         bt[b, : npages[b]] = perm[i: i + npages[b]].to(torch.int32)
         i += npages[b]
-    KVH = k.shape[1]
-    k_pool = torch.zeros(P, KVH, PAGE, D, dtype=k.dtype, device=device)
+    KVH, HD = k.shape[1], k.shape[2]
+    k_pool = torch.zeros(P, KVH, PAGE, HD, dtype=k.dtype, device=device)
     v_pool = torch.zeros_like(k_pool)
     # token t of sequence b -> (page bt[b, t//16], slot t%16)
     starts = [0]
@@ -118,12 +118,12 @@ def varlen_to_paged(k, v, lens, pool_factor=1.25, seed=0, max_blocks=None):
         t = torch.arange(L)
         phys_rows[starts[b]: starts[b] + L] = bt[b, (t // PAGE)].to(torch.int64) * PAGE + t % PAGE
     phys_rows = phys_rows.to(device)
-    kf = k_pool.permute(0, 2, 1, 3).reshape(P * PAGE, KVH, D)
-    vf = v_pool.permute(0, 2, 1, 3).reshape(P * PAGE, KVH, D)
+    kf = k_pool.permute(0, 2, 1, 3).reshape(P * PAGE, KVH, HD)
+    vf = v_pool.permute(0, 2, 1, 3).reshape(P * PAGE, KVH, HD)
     kf.index_copy_(0, phys_rows, k)
     vf.index_copy_(0, phys_rows, v)
-    k_pool = kf.reshape(P, PAGE, KVH, D).permute(0, 2, 1, 3).contiguous()
-    v_pool = vf.reshape(P, PAGE, KVH, D).permute(0, 2, 1, 3).contiguous()
+    k_pool = kf.reshape(P, PAGE, KVH, HD).permute(0, 2, 1, 3).contiguous()
+    v_pool = vf.reshape(P, PAGE, KVH, HD).permute(0, 2, 1, 3).contiguous()
     return k_pool, v_pool, bt.to(device)
 
 

@@ -14,7 +14,11 @@
  * Conventions shared by every entry point
  *  - All pointers are device pointers except `stream` (a cudaStream_t passed
  *    as void*; NULL = legacy default stream).  Strides are in ELEMENTS.
- *  - head_dim must be 128, q_heads % kv_heads == 0 and G <= 8.
+ *  - head_dim D is 128, or 64 with f16/bf16 KV (the reference's Triton
+ *    kernels take any power of two, triton_gqa_decode.py:136-152; its native
+ *    kernel only 128, flash_decode_cuda.cu:168-189).  q_heads % kv_heads
+ *    == 0; any group size G = q_heads / kv_heads.  Shapes below write D
+ *    as 128.
  *  - The innermost (head_dim) stride of every tensor is 1; K/V base pointers
  *    and their strides in bytes must be multiples of 16 (TMA rule).
  *  - Nothing is synchronised with the host and nothing is allocated: the
@@ -24,7 +28,7 @@
  *    that each launch leaves at zero; calls sharing a workspace must be
  *    stream-ordered, and a new workspace must start zeroed.
  *  - `workspace` is caller-owned device memory of at least
- *    fk_decode_workspace_bytes(...) bytes.  Its first int32 is a sticky
+ *    fk_decode_workspace_bytes_gqa(...) bytes.  Its first int32 is a sticky
  *    status word (FK_STATUS_*) that kernels OR into; the caller clears it.
  *  - Return value: FK_OK or an FK_ERR_* code; fk_last_error() describes it.
  */

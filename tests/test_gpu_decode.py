@@ -614,3 +614,71 @@ def test_fp8_large_groups_paged_and_dense(dev, G):
     outd = fk.flash_decode_gqa_hf_fp8(q, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), sl, None, sk, sv,
                                       torch.float16, s_aux=d["s_aux"])
     assert torch.equal(outd, outp)
+
+
+# ------------------------------------------------------------- head dim 64
+# The reference's Triton kernels take any power-of-two head dim
+# (triton_gqa_decode.py:136-152); 64 is served here for 16-bit KV.
+def _rand_case_d(dev, lens, qh, kvh, dtype, sinks, seed, head_dim):
+    d = W.make_varlen(lens, qh, kvh, torch.float32, dev, seed=seed, sinks=sinks, head_dim=head_dim)
+    return d["q"].to(dtype), d["k"].to(dtype), d["v"].to(dtype), d["cu_seqlens"], d["s_aux"]
+
+
+@pytest.mark.parametrize("G,kvh", [(1, 8), (4, 8), (8, 8), (8, 3), (16, 4)])
+@pytest.mark.parametrize("sinks", [False, True])
+def test_head_dim_64_varlen(dev, G, kvh, sinks):
+    lens = [1, 15, 16, 17, 64, 700, 0, 9001]
+    q, k, v, cu, s = _rand_case_d(dev, lens, G * kvh, kvh, torch.float16, sinks, 100 + G, 64)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    assert out.shape == q.shape
+    close(out, _oracle(q, k, v, cu, s), **F16_TOL)
+    assert N.read_status(dev) == 0
+
+
+def test_head_dim_64_bf16_paged_dense_and_varlen_agree(dev):
+    lens = [3000, 1, 0, 12000, 257, 64]
+    B = len(lens)
+    q, k, v, cu, s = _rand_case_d(dev, lens, 64, 8, torch.bfloat16, True, 7, 64)
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    close(out, _oracle(q, k, v, cu, s), **BF16_TOL)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    kp, vp, bt = W.varlen_to_paged(k, v, lens, 1.25, seed=5)
+    outp = fk.paged_flash_decode(q, kp, vp, bt, sl, 16, s_aux=s)
+    assert torch.equal(out, outp)
+    S = max(lens)
+    kc = torch.zeros(B, 8, S, 64, dtype=k.dtype, device=dev)
+    vc = torch.zeros_like(kc)
+    c = cu.tolist()
+    for b, L in enumerate(lens):
+        kc[b, :, :L] = k[c[b]:c[b + 1]].transpose(0, 1)
+        vc[b, :, :L] = v[c[b]:c[b + 1]].transpose(0, 1)
+    outd = fk.flash_decode_gqa_hf_dense_optimized(q, kc, vc, sl, s_aux=s)
+    assert torch.equal(out, outd)
+    # a sliding window on the dense cache
+    st = torch.tensor([0, 0, 0, 11000, 200, 10], dtype=torch.int32, device=dev)
+    outw = fk.flash_decode_gqa_hf_dense_optimized(q, kc, vc, sl, st, s_aux=s)
+    ref = O.decode_dense(q.float().cpu().numpy(), kc.float().cpu().numpy(), vc.float().cpu().numpy(),
+                         lens, st.cpu().numpy(), s.cpu().numpy())
+    close(outw, ref, **BF16_TOL)
+
+
+def test_head_dim_64_append_then_decode(dev):
+    B, KVH, P = 4, 8, 64
+    g = torch.Generator(device=dev).manual_seed(9)
+    k_new = torch.randn(B, KVH, 64, generator=g, device=dev).half()
+    v_new = torch.randn(B, KVH, 64, generator=g, device=dev).half()
+    kp = torch.zeros(P, KVH, 16, 64, device=dev, dtype=torch.float16)
+    vp = torch.zeros_like(kp)
+    bt = torch.randperm(P, generator=torch.Generator().manual_seed(2))[:B * 4].view(B, 4).to(torch.int32).to(dev)
+    pos = torch.tensor([0, 15, 16, 40], dtype=torch.int32, device=dev)
+    fk.paged_attn.paged_kv_append(k_new, v_new, kp, vp, bt, pos, increment=True)
+    torch.cuda.synchronize()
+    assert pos.tolist() == [1, 16, 17, 41]
+    for b, p0 in enumerate([0, 15, 16, 40]):
+        phys = int(bt[b, p0 // 16])
+        assert torch.equal(kp[phys, :, p0 % 16], k_new[b])
+        assert torch.equal(vp[phys, :, p0 % 16], v_new[b])
+    with pytest.raises(ValueError):
+        fk.paged_flash_decode(torch.zeros(B, 32, 64, device=dev, dtype=torch.float16), kp.view(torch.uint8)[..., :64]
+                              .view(torch.float8_e4m3fn), kp.view(torch.uint8)[..., :64].view(torch.float8_e4m3fn),
+                              bt, pos, 16)

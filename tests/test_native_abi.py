@@ -43,7 +43,7 @@ def test_invalid_arguments_are_rejected_without_touching_the_device():
                                       0, 0, 0, 0, 0, 0, 0, 0, None, 0, None)
     assert rc == 1 and "non-null" in N.last_error()
     fake = ctypes.c_void_p(16)
-    rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 32, 8, 64, 16, 0,
+    rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 32, 8, 96, 16, 0,
                                       0, 0, 0, 0, 0, 0, 0, 0, fake, 0, None)
     assert rc == 2 and "head_dim" in N.last_error()
     rc = L.fk_flash_decode_gqa_varlen(fake, fake, fake, fake, None, fake, 1, 36, 8, 128, 16, 0,
