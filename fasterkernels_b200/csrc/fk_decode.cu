@@ -70,6 +70,9 @@ constexpr float NEG_INF = -__builtin_huge_valf();
 enum Layout { VARLEN = 0, DENSE = 1, PAGED = 2 };
 enum Flags { F_FIRST = 1, F_LAST = 2, F_WHOLE = 4, F_END = 8 };
 
+#ifndef FK_D64_STAGES
+#define FK_D64_STAGES 8
+#endif
 // Per KV element type and head dim D (128; 64 for 16-bit KV).
 template <int KV, int D>
 struct KvCfg {
@@ -81,7 +84,8 @@ struct KvCfg {
   static constexpr int KD = D / 16;                          // MMA k-steps (QK) / dim tiles (PV)
   static constexpr int TILE_BYTES = TILE * D * ES;           // K (or V) bytes per stage
   static constexpr int PAGE_BYTES = PAGE * D * ES;           // one page of K (or V)
-  static constexpr int STAGES = FP8 ? 4 : 5;
+  // D = 64 stages carry half the bytes: more of them keep as many in flight
+  static constexpr int STAGES = FP8 ? 4 : (D == 64 ? FK_D64_STAGES : 5);
   static constexpr int NSLOT = FP8 ? 1 : 2;                  // epilogue slots (smem budget: 2 CTAs/SM for FP8)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int MINB = FP8 ? 2 : 1;                   // resident CTAs per SM (at least)
