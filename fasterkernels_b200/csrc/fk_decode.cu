@@ -54,7 +54,6 @@ namespace fk {
 
 constexpr int HEAD_DIM = 128;  // largest head dim; workspace records, epilogue slots and Q rows are sized for it
 constexpr int GPAD = 8;        // MMA N: query heads of one KV group, padded
-constexpr int TILE = 64;       // tokens per pipeline stage
 constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
 constexpr int EWARPS = 2;      // epilogue warps: segment merge / output / partials
 constexpr int THREADS = (CWARPS + 1 + EWARPS) * 32;
@@ -70,9 +69,6 @@ constexpr float NEG_INF = -__builtin_huge_valf();
 enum Layout { VARLEN = 0, DENSE = 1, PAGED = 2 };
 enum Flags { F_FIRST = 1, F_LAST = 2, F_WHOLE = 4, F_END = 8 };
 
-#ifndef FK_D64_STAGES
-#define FK_D64_STAGES 8
-#endif
 // Per KV element type and head dim D (128; 64 for 16-bit KV).
 template <int KV, int D>
 struct KvCfg {
@@ -82,10 +78,13 @@ struct KvCfg {
   static constexpr int ES = FP8 ? 1 : 2;                     // bytes per element
   static constexpr int NH = D * ES / 128;                    // 128-byte halves per row
   static constexpr int KD = D / 16;                          // MMA k-steps (QK) / dim tiles (PV)
+  // Rows (tokens x item heads) per stage: D = 64 doubles them so that a stage
+  // carries as many bytes as at D = 128; each consumer warp then takes
+  // TILE / 64 blocks of 16 rows.
+  static constexpr int TILE = (D == 64) ? 128 : 64;
   static constexpr int TILE_BYTES = TILE * D * ES;           // K (or V) bytes per stage
   static constexpr int PAGE_BYTES = PAGE * D * ES;           // one page of K (or V)
-  // D = 64 stages carry half the bytes: more of them keep as many in flight
-  static constexpr int STAGES = FP8 ? 4 : (D == 64 ? FK_D64_STAGES : 5);
+  static constexpr int STAGES = FP8 ? 4 : 5;
   static constexpr int NSLOT = FP8 ? 1 : 2;                  // epilogue slots (smem budget: 2 CTAs/SM for FP8)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int MINB = FP8 ? 2 : 1;                   // resident CTAs per SM (at least)
@@ -112,7 +111,7 @@ template <int KV, int LAYOUT, int HP, int D>
 struct TileLayout {
   static constexpr bool PG = LAYOUT == 2;  // PAGED
   static constexpr int NH = KvCfg<KV, D>::NH;
-  static constexpr int TT = TILE / HP;
+  static constexpr int TT = KvCfg<KV, D>::TILE / HP;
   static constexpr uint32_t HALF_STRIDE = PG ? 2048u : uint32_t(TT * 128);
   __device__ static __forceinline__ uint32_t row_off(int hh, int r) {
     if constexpr (PG) return uint32_t((r >> 4) * (HP * NH * 2048) + hh * (NH * 2048) + (r & 15) * 128);
@@ -331,7 +330,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
   using C = KvCfg<KV, D>;
   using TL = TileLayout<KV, LAYOUT, HP, D>;
   constexpr int KD = C::KD;
-  constexpr int TT = TILE / HP;          // tokens per KV head in one stage
+  constexpr int TT = C::TILE / HP;       // tokens per KV head in one stage
   constexpr int WPH = CWARPS / HP;       // consumer warps per KV head
   constexpr int PPT = TT / PAGE;         // pages per KV head in one stage
   constexpr int QWORDS = HP * GPAD * 64; // staged Q words per stage
@@ -957,10 +956,16 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
       }
     }
 
-    if (r0 < mt.valid) {
+    // Blocks of 16 rows of this warp in the stage (two at D = 64).
+    constexpr int NBLK = C::TILE / 64;
+#pragma unroll
+    for (int blk = 0; blk < NBLK; ++blk) {
+      const int bo = blk * (WPH * 16);  // row offset of the block
+      const int r0b = r0 + bo;
+      if (r0b >= mt.valid) break;
       const uint32_t sK = smem_u32(stages + stage * C::STAGE_BYTES);
       const uint32_t sV = sK + C::TILE_BYTES;
-      const bool partial = (r0 + 16 > mt.valid) || (mt.bad != 0);
+      const bool partial = (r0b + 16 > mt.valid) || (mt.bad != 0);
       auto tok_ok = [&](int row) -> bool { return row < mt.valid && !((mt.bad >> (row >> 4)) & 1); };
 
       // ---- S^T = K Q^T : 16 tokens x 8 heads
@@ -968,10 +973,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
       float s2[4] = {0.f, 0.f, 0.f, 0.f};  // odd k-steps: two independent MMA chains
       int rowA, rowB;
       if constexpr (FP8) {
-        rowA = prow;
-        rowB = prow + 8;
-        const int sw = prow & 7;
-        const uint32_t ra = sK + TL::row_off(hk, prow), rb = ra + 8 * 128;
+        rowA = (prow + bo);
+        rowB = (prow + bo) + 8;
+        const int sw = (prow + bo) & 7;
+        const uint32_t ra = sK + TL::row_off(hk, (prow + bo)), rb = ra + 8 * 128;
         const uint4 alo = lds128(ra + ((t ^ sw) << 4));
         const uint4 ahi = lds128(ra + (((t + 4) ^ sw) << 4));
         const uint4 blo = lds128(rb + ((t ^ sw) << 4));
@@ -988,10 +993,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
           else mma16816<false>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
         }
       } else {
-        rowA = r0 + g;
-        rowB = r0 + g + 8;
-        const uint32_t kb = sK + TL::row_off(hk, krow);
-        const int ksw = krow & 7;
+        rowA = r0b + g;
+        rowB = r0b + g + 8;
+        const uint32_t kb = sK + TL::row_off(hk, (krow + bo));
+        const int ksw = (krow + bo) & 7;
 #pragma unroll
         for (int j = 0; j < KD; ++j) {
           const int c = ((j & 3) << 1) + (lq >> 1);
@@ -1042,7 +1047,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
         uint4 x[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          const int row = r0 + t + 4 * (r & 1) + 8 * (r >> 1);
+          const int row = r0b + t + 4 * (r & 1) + 8 * (r >> 1);
           x[r] = lds128(sV + TL::row_off(hk, row) + ((cg ^ (row & 7)) << 4));
           if (partial && !tok_ok(row)) x[r] = make_uint4(0u, 0u, 0u, 0u);
         }
@@ -1061,12 +1066,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
       } else {
         uint32_t mk01 = 0xffffffffu, mk89 = 0xffffffffu;
         if (partial) {
-          const int tk = r0 + 2 * t;
+          const int tk = r0b + 2 * t;
           mk01 = (tok_ok(tk) ? 0x0000ffffu : 0u) | (tok_ok(tk + 1) ? 0xffff0000u : 0u);
           mk89 = (tok_ok(tk + 8) ? 0x0000ffffu : 0u) | (tok_ok(tk + 9) ? 0xffff0000u : 0u);
         }
-        const uint32_t vb = sV + TL::row_off(hk, vrow);
-        const int vsw = vrow & 7;
+        const uint32_t vb = sV + TL::row_off(hk, (vrow + bo));
+        const int vsw = (vrow + bo) & 7;
 #pragma unroll
         for (int i = 0; i < KD; ++i) {
           const int c = ((2 * i) & 7) + (lq & 1);
@@ -1208,6 +1213,11 @@ inline int hp_for(int kv_heads, int qc = 1) {
   if (forced == 1) return 1;
   if (qc > 1) return 2;  // chunk pairs of one KV head
   return (kv_heads % 2 == 0) ? 2 : 1;
+}
+
+// Rows per pipeline stage (tokens x item heads) of the kernel for (kv, D).
+inline uint32_t tile_rows(int kv, int head_dim) {
+  return (kv != FK_DTYPE_E4M3 && head_dim == 64) ? 128u : 64u;
 }
 
 // KV heads in one TMA box: chunk pairs load a single head.
@@ -1541,7 +1551,7 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
   // box {64, 64/hp, D/64, hp} per stage lands as [head][half][rows][64].
   const uint32_t nh = static_cast<uint32_t>(head_dim / 64);
   const uint64_t dims[4] = {64, T, nh, static_cast<uint64_t>(kv_heads)};
-  const uint32_t box[4] = {64, TILE / hp, nh, hb};
+  const uint32_t box[4] = {64, tile_rows(dtype, head_dim) / hp, nh, hb};
   const uint64_t ks[3] = {static_cast<uint64_t>(sk_t) * 2, 128, static_cast<uint64_t>(sk_h) * 2};
   const uint64_t vs[3] = {static_cast<uint64_t>(sv_t) * 2, 128, static_cast<uint64_t>(sv_h) * 2};
   if ((rc = encode_map(&p.tk, dtype, 4, k_varlen, dims, ks, box)) != FK_OK) return rc;
@@ -1582,7 +1592,7 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
   if (kv_dtype == FK_DTYPE_E4M3) {
     // (128 dims, S rows, heads, batch): box {128, 64/hp, hp, 1} -> [head][rows][128]
     const uint64_t dims[4] = {HEAD_DIM, static_cast<uint64_t>(max_seqlen), static_cast<uint64_t>(kv_heads), Bd};
-    const uint32_t box[4] = {128, TILE / hp, hb, 1};
+    const uint32_t box[4] = {128, tile_rows(kv_dtype, head_dim) / hp, hb, 1};
     const uint64_t ks[3] = {static_cast<uint64_t>(sk_s), static_cast<uint64_t>(sk_h), static_cast<uint64_t>(sk_b)};
     const uint64_t vs[3] = {static_cast<uint64_t>(sv_s), static_cast<uint64_t>(sv_h), static_cast<uint64_t>(sv_b)};
     if ((rc = encode_map(&p.tk, kv_dtype, 4, k_cache, dims, ks, box)) != FK_OK) return rc;
@@ -1592,7 +1602,7 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
     // -> [head][half][rows][64]
     const uint32_t nh = static_cast<uint32_t>(head_dim / 64);
     const uint64_t dims[5] = {64, static_cast<uint64_t>(max_seqlen), nh, static_cast<uint64_t>(kv_heads), Bd};
-    const uint32_t box[5] = {64, TILE / hp, nh, hb, 1};
+    const uint32_t box[5] = {64, tile_rows(kv_dtype, head_dim) / hp, nh, hb, 1};
     const uint64_t ks[4] = {static_cast<uint64_t>(sk_s) * 2, 128, static_cast<uint64_t>(sk_h) * 2,
                             static_cast<uint64_t>(sk_b) * 2};
     const uint64_t vs[4] = {static_cast<uint64_t>(sv_s) * 2, 128, static_cast<uint64_t>(sv_h) * 2,
