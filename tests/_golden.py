@@ -23,4 +23,9 @@ def e4m3_to_float(u8):
 
 
 def varlen_cases():
-    return ["varlen_g4_nosink", "varlen_g4_sink", "varlen_g4_sink01", "varlen_g8_sink", "varlen_edge_sink"]
+    return ["varlen_g4_nosink", "varlen_g4_sink", "varlen_g4_sink01", "varlen_g8_sink", "varlen_edge_sink",
+            "varlen_g16_nosink", "varlen_g8_d64_nosink", "varlen_g4_d64_sink"]
+
+
+def paged_cases():
+    return ["paged_g4", "paged_g4_d64"]

@@ -15,7 +15,8 @@ interpreter (TRITON_INTERPRET=1):
   K6 paged_flash_decode            fskernels/paged_attn/triton_paged_attn.py:96-125
 Inputs are drawn from a seeded torch.Generator on the CPU and stored with the
 outputs, so the fixtures need no reference at test time.  Sizes are kept
-small (KV heads 2) so the files stay a few hundred KB each.
+small (KV heads 2) so the files stay a few hundred KB each.  Names given on
+the command line regenerate only those fixtures.
 """
 from __future__ import annotations
 
@@ -44,7 +45,7 @@ D = 128
 def padded_from_varlen(k, cu, B, KVH):
     lens = (cu[1:] - cu[:-1]).tolist()
     S = max(max(lens), 1)
-    kp = torch.zeros(B, KVH, S, D, dtype=torch.float32)
+    kp = torch.zeros(B, KVH, S, k.shape[-1], dtype=torch.float32)
     for b in range(B):
         kp[b, :, : lens[b]] = k[cu[b]: cu[b + 1]].float().transpose(0, 1)
     return kp
@@ -56,15 +57,15 @@ def oracle_ref(q, kp, vp, lens, QH, sink):
     return out
 
 
-def varlen_case(name, seed, lens, QH, KVH, sink_scale, run_kernel):
+def varlen_case(name, seed, lens, QH, KVH, sink_scale, run_kernel, hd=D):
     g = torch.Generator().manual_seed(seed)
     B = len(lens)
     cu = torch.zeros(B + 1, dtype=torch.int32)
     cu[1:] = torch.cumsum(torch.tensor(lens), 0).to(torch.int32)
     T = int(cu[-1])
-    q = torch.randn(B, QH, D, generator=g).half()
-    k = torch.randn(T, KVH, D, generator=g).half()
-    v = torch.randn(T, KVH, D, generator=g).half()
+    q = torch.randn(B, QH, hd, generator=g).half()
+    k = torch.randn(T, KVH, hd, generator=g).half()
+    v = torch.randn(T, KVH, hd, generator=g).half()
     sink = None if sink_scale is None else (torch.randn(QH, generator=g) * sink_scale).float()
     kp, vp = padded_from_varlen(k, cu, B, KVH), padded_from_varlen(v, cu, B, KVH)
     ref = oracle_ref(q, kp, vp, lens, QH, sink)
@@ -78,15 +79,15 @@ def varlen_case(name, seed, lens, QH, KVH, sink_scale, run_kernel):
           float(np.abs(rec["ref_kernel"] - rec["ref"]).max()) if run_kernel else "-")
 
 
-def paged_case(name, seed, lens, QH, KVH, extra_pages):
+def paged_case(name, seed, lens, QH, KVH, extra_pages, hd=D):
     g = torch.Generator().manual_seed(seed)
     B = len(lens)
     PS = 16
-    q = torch.randn(B, QH, D, generator=g).half()
+    q = torch.randn(B, QH, hd, generator=g).half()
     npages = [(L + PS - 1) // PS for L in lens]
     P = sum(npages) + extra_pages
-    k_pool = torch.randn(P, KVH, PS, D, generator=g).half()
-    v_pool = torch.randn(P, KVH, PS, D, generator=g).half()
+    k_pool = torch.randn(P, KVH, PS, hd, generator=g).half()
+    v_pool = torch.randn(P, KVH, PS, hd, generator=g).half()
     perm = torch.randperm(P, generator=g)
     maxb = max(npages) + 1
     bt = torch.full((B, maxb), -1, dtype=torch.int32)
@@ -96,8 +97,8 @@ def paged_case(name, seed, lens, QH, KVH, extra_pages):
             bt[b, p] = int(perm[i])
             i += 1
     S = max(lens)
-    kp = torch.zeros(B, KVH, S, D)
-    vp = torch.zeros(B, KVH, S, D)
+    kp = torch.zeros(B, KVH, S, hd)
+    vp = torch.zeros(B, KVH, S, hd)
     for b in range(B):
         for p in range(npages[b]):
             n = min(PS, lens[b] - p * PS)
@@ -179,14 +180,25 @@ def config1_case():
     print("config1 lens", lens.tolist())
 
 
+CASES = {
+    "varlen_g4_nosink": lambda: varlen_case("varlen_g4_nosink", 1, [37, 1, 200], 8, 2, None, True),
+    "varlen_g4_sink": lambda: varlen_case("varlen_g4_sink", 2, [37, 1, 200], 8, 2, 1.0, True),
+    "varlen_g4_sink01": lambda: varlen_case("varlen_g4_sink01", 3, [130, 64, 17], 8, 2, 0.1, True),
+    "varlen_g8_sink": lambda: varlen_case("varlen_g8_sink", 4, [65, 130], 16, 2, 1.0, False),
+    "varlen_edge_sink": lambda: varlen_case("varlen_edge_sink", 5, [0, 5, 16, 17, 0], 8, 2, 1.0, False),
+    "paged_g4": lambda: paged_case("paged_g4", 6, [64, 33, 250, 17], 8, 2, 7),
+    "dense_g4_window": lambda: dense_case("dense_g4_window", 7, 2, 8, 2, 96, [90, 50], [10, 0], 4),
+    "fp8_g4": lambda: fp8_case("fp8_g4", 8, 2, 8, 2, 160, [150, 77], 2),
+    "config1": config1_case,
+    # shapes beyond BASELINE's: a 16-head group (K1 pads it to BLOCK_H = 16)
+    # and head dim 64 (K1 and K6 take any power of two)
+    "varlen_g16_nosink": lambda: varlen_case("varlen_g16_nosink", 9, [70, 1, 150], 32, 2, None, True),
+    "varlen_g8_d64_nosink": lambda: varlen_case("varlen_g8_d64_nosink", 10, [90, 3, 200], 16, 2, None, True, hd=64),
+    "varlen_g4_d64_sink": lambda: varlen_case("varlen_g4_d64_sink", 11, [90, 0, 33], 8, 2, 1.0, False, hd=64),
+    "paged_g4_d64": lambda: paged_case("paged_g4_d64", 12, [64, 33, 250, 17], 8, 2, 7, hd=64),
+}
+
 if __name__ == "__main__":
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    varlen_case("varlen_g4_nosink", 1, [37, 1, 200], 8, 2, None, True)
-    varlen_case("varlen_g4_sink", 2, [37, 1, 200], 8, 2, 1.0, True)
-    varlen_case("varlen_g4_sink01", 3, [130, 64, 17], 8, 2, 0.1, True)
-    varlen_case("varlen_g8_sink", 4, [65, 130], 16, 2, 1.0, False)
-    varlen_case("varlen_edge_sink", 5, [0, 5, 16, 17, 0], 8, 2, 1.0, False)
-    paged_case("paged_g4", 6, [64, 33, 250, 17], 8, 2, 7)
-    dense_case("dense_g4_window", 7, 2, 8, 2, 96, [90, 50], [10, 0], 4)
-    fp8_case("fp8_g4", 8, 2, 8, 2, 160, [150, 77], 2)
-    config1_case()
+    for name in (sys.argv[1:] or list(CASES)):
+        CASES[name]()

@@ -13,7 +13,7 @@ import fasterkernels_b200 as fk
 from fasterkernels_b200 import _native as N
 from fasterkernels_b200 import workloads as W
 from oracle import gqa_decode_oracle as O
-from tests._golden import e4m3_to_float, load, varlen_cases
+from tests._golden import e4m3_to_float, load, paged_cases, varlen_cases
 
 pytestmark = pytest.mark.gpu
 F16_TOL = dict(atol=2e-3, rtol=1e-2)
@@ -46,8 +46,9 @@ def test_varlen_golden(dev, name):
     assert N.read_status(dev) == 0
 
 
-def test_paged_golden_and_bit_identity(dev):
-    z = load("paged_g4")
+@pytest.mark.parametrize("name", paged_cases())
+def test_paged_golden_and_bit_identity(dev, name):
+    z = load(name)
     q = t(z["q"], dev)
     kp, vp, bt, sl = t(z["k_pool"], dev), t(z["v_pool"], dev), t(z["block_table"], dev), t(z["seq_lens"], dev)
     out = fk.paged_flash_decode(q, kp, vp, bt, sl, 16)

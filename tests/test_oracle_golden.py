@@ -16,9 +16,11 @@ def test_varlen_oracle_matches_reference_ref_attention(name):
     np.testing.assert_allclose(out, z["ref"], atol=2e-5, rtol=1e-5)
 
 
-def test_varlen_oracle_matches_reference_triton_kernel_without_sinks():
-    # K1 (triton_gqa_decode.py:35-122) run by the Triton interpreter, fp16 output
-    z = load("varlen_g4_nosink")
+@pytest.mark.parametrize("name", ["varlen_g4_nosink", "varlen_g16_nosink", "varlen_g8_d64_nosink"])
+def test_varlen_oracle_matches_reference_triton_kernel_without_sinks(name):
+    # K1 (triton_gqa_decode.py:35-122) run by the Triton interpreter, fp16
+    # output; a 16-head group and head dim 64 included
+    z = load(name)
     out = O.decode_varlen(z["q"], z["k"], z["v"], z["cu_seqlens"])
     np.testing.assert_allclose(out, z["ref_kernel"], atol=2e-3, rtol=1e-2)
 
@@ -43,8 +45,9 @@ def test_edge_case_zero_length_rows_are_zero():
     np.testing.assert_allclose(out, z["ref"], atol=2e-5, rtol=1e-5)
 
 
-def test_paged_oracle_matches_reference():
-    z = load("paged_g4")
+@pytest.mark.parametrize("name", ["paged_g4", "paged_g4_d64"])
+def test_paged_oracle_matches_reference(name):
+    z = load(name)
     out = O.decode_paged(z["q"], z["k_pool"], z["v_pool"], z["block_table"], z["seq_lens"])
     np.testing.assert_allclose(out, z["ref"], atol=2e-5, rtol=1e-5)
     # K6 (triton_paged_attn.py:19-93) under the Triton interpreter
