@@ -2,11 +2,12 @@
 // kernel (split-KV pass with an in-kernel sink-aware merge), behind the C-ABI
 // declared in include/fk_decode.h.
 //
-// Work decomposition ("stream-K" over KV granules).  Every (sequence b,
-// KV head h) pair is an item owning ceil(len_b / 16) granules of 16 tokens;
-// items are laid end to end (b-major, h minor) into one stream of
-// U = kv_heads * sum_b ceil(len_b/16) granules, and CTA c of the persistent
-// grid (S CTAs, S = resident CTAs on the device) takes granules
+// Work decomposition ("stream-K" over KV granules).  A work item is one
+// sequence b x HP KV heads (HP = 2 when kv_heads is even), or, for groups of
+// more than 8 query heads, one KV head x two chunks of at most 8 query heads.
+// Each item owns ceil(len_b / 16) granules of 16 tokens; items are laid end
+// to end (b-major) into one stream of U granules, and CTA c of the
+// persistent grid (S CTAs, S = resident CTAs on the device) takes granules
 // [c*per, (c+1)*per) with per = max(ceil(U/S), 4).  Every CTA therefore
 // streams the same number of KV bytes whatever the length distribution, and
 // the plan is derived on the device from the lengths alone (no host sync,
@@ -18,20 +19,22 @@
 // CTA order with the sink term (log-sum-exp combine) and re-arms the counter.
 // One launch per decode call; no CTA ever waits for another.
 //
-// Split pass, per CTA: one producer warp walks the plan and issues TMA tile
-// loads (64 tokens x 128 dims of K and of V per stage, 128-byte swizzled)
-// into an mbarrier ring; four consumer warps each take 16 tokens of every
+// Split pass, per CTA: one producer warp walks the plan, copies each
+// segment's Q rows with cp.async and issues TMA tile loads (64 rows, or 128
+// at head dim 64, of K and of V per stage, 128-byte swizzled) into an
+// mbarrier ring; four consumer warps each take blocks of 16 rows of every
 // tile and run QK^T and PV on the tensor cores with mma.sync m16n8k16,
-// tokens as the M dimension and up to 8 query heads of the KV group as N (a
-// larger group is split into items of at most 8 query heads),
-// keeping a private online-softmax state that is merged across the warps at
-// the end of each segment.  FP8 e4m3 K/V are widened to f16 in registers;
-// scale_k folds into the logit scale and scale_v into the final output.
+// tokens as the M dimension and up to 8 query heads as N, keeping a private
+// online-softmax state; two epilogue warps merge the four warps' states of
+// each finished segment and write outputs or partials.  FP8 e4m3 K/V are
+// widened to f16 in registers; scale_k folds into the logit scale and
+// scale_v into the final output.
 //
-// Layouts (address policies of the producer):
-//   VARLEN  k[T, KVH, 128]          3-D tensor map, coords (d, h, t)
-//   DENSE   k[B, KVH, S, 128]       4-D tensor map, coords (d, s, h, b)
-//   PAGED   pool[P, KVH, 16, 128]   4-D tensor map, coords (d, 0, h, page)
+// Layouts (address policies of the producer; D = head dim, 128 or 64):
+//   VARLEN  k[T, KVH, D]          tensor map coords (d, t, half, h)
+//   DENSE   k[B, KVH, S, D]       tensor map coords (d, s, half, h, b)
+//   PAGED   pool[P, KVH, 16, D]   tensor map coords (d, slot, half, h, page)
+// (e4m3 rows are a single 128-byte half, so their maps drop that coordinate.)
 // The plan, the tile sequence and the arithmetic do not depend on the
 // layout, so paged and contiguous results are bit-identical.
 #include <cuda.h>
@@ -637,7 +640,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
           __syncwarp();
           if constexpr (LAYOUT == PAGED) {
             if (phys >= 0) {
-              // one box per page: 16 tokens x HP heads x 128 dims
+              // one box per page: 16 tokens x HP heads x D dims
               const uint32_t off = lane * (HP * C::PAGE_BYTES);
               if constexpr (C::FP8) {
                 tma_load_4d(sK + off, &p.tk, fb, 0, 0, hcoord, phys);
@@ -648,7 +651,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
               }
             }
           } else if (lane == 0) {
-            // one box per stage: TT tokens x HP heads x 128 dims
+            // one box per stage: TT tokens x HP heads x D dims
             const int row = static_cast<int>(tok0 + tt);
             if constexpr (LAYOUT == VARLEN) {
               if constexpr (C::FP8) {
@@ -1042,7 +1045,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
       const uint32_t pb0 = movmatrix_t(pack2<MBF16>(p0, p1));
       const uint32_t pb1 = movmatrix_t(pack2<MBF16>(p2, p3));
 
-      // ---- O^T += V^T P^T : 128 dims x 8 heads
+      // ---- O^T += V^T P^T : D dims x 8 heads
       if constexpr (FP8) {
         uint4 x[4];
 #pragma unroll
