@@ -1034,12 +1034,16 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
       l[1] = l[1] * al1 + (p1 + p3);
       m[0] = mn0;
       m[1] = mn1;
+      // Rescale only when some running max of the warp moved (after the first
+      // tiles it rarely does); a factor of exactly 1 would leave acc as is.
+      if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
 #pragma unroll
-      for (int i = 0; i < KD; ++i) {
-        acc[i][0] *= al0;
-        acc[i][1] *= al1;
-        acc[i][2] *= al0;
-        acc[i][3] *= al1;
+        for (int i = 0; i < KD; ++i) {
+          acc[i][0] *= al0;
+          acc[i][1] *= al1;
+          acc[i][2] *= al0;
+          acc[i][3] *= al1;
+        }
       }
       // P^T as the B operand: transpose the 8x8 (token x head) blocks.
       const uint32_t pb0 = movmatrix_t(pack2<MBF16>(p0, p1));
