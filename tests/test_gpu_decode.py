@@ -569,7 +569,7 @@ def test_paged_strided_block_table(dev):
 # The reference's Triton kernels take any group size (BLOCK_H pads it,
 # fskernels/triton/triton_gqa_decode.py:132); here a group of more than 8
 # query heads is split into items of at most 8 sharing the KV head.
-@pytest.mark.parametrize("G,kvh", [(9, 4), (12, 8), (16, 8), (32, 2)])
+@pytest.mark.parametrize("G,kvh", [(9, 4), (12, 8), (16, 8), (20, 2), (32, 2)])
 @pytest.mark.parametrize("sinks", [False, True])
 def test_varlen_large_groups(dev, G, kvh, sinks):
     lens = [1, 17, 64, 700, 0, 5000, 12345]
