@@ -20,7 +20,8 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libfk_decode.so")
 SOURCES = [os.path.join(CSRC, "fk_decode.cu"), os.path.join(CSRC, "fk_paged_append.cu")]
-DEPS = SOURCES + [os.path.join(CSRC, "fk_ptx.cuh"), os.path.join(REPO_DIR, "include", "fk_decode.h")]
+DEPS = SOURCES + [os.path.join(CSRC, "fk_ptx.cuh"), os.path.join(CSRC, "fk_decode_kernel.cuh"),
+                  os.path.join(REPO_DIR, "include", "fk_decode.h")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
