@@ -20,7 +20,8 @@ from typing import Optional, Tuple
 import torch
 
 from .gqa_decode import HEAD_DIM
-from .gqa_decode_hf import _decode_window, _fallback, _is_decode, _module_sinks, dense_decode
+from .gqa_decode_hf import (_decode_window, _fallback, _is_decode, _module_sinks, custom_hf_decode_attention_forward,
+                            dense_decode)
 
 FP8_DTYPE = torch.float8_e4m3fn
 FP8_MAX = 448.0
@@ -65,8 +66,13 @@ def custom_hf_decode_attention_forward_fp8(module, query_states, key_states, val
                                            **kwargs) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """As the reference adapter (:230-283): quantise Q, K and V per call with
     per-tensor scales, then decode.  A cache that is already e4m3 (with
-    ``module.k_scale``/``module.v_scale`` tensors) is used without re-quantising."""
+    ``module.k_scale``/``module.v_scale`` tensors) is used without re-quantising.
+    e4m3 KV runs at head dim 128 only: a 16-bit cache of another head dim
+    decodes in 16 bits (custom_hf_decode_attention_forward) instead."""
     bsz, q_heads, q_len, head_dim = query_states.shape
+    if head_dim != HEAD_DIM and key_states.dtype != FP8_DTYPE:
+        return custom_hf_decode_attention_forward(module, query_states, key_states, value_states, attention_mask,
+                                                  scaling, dropout, **kwargs)
     if _is_decode(kwargs, query_states):
         out_dtype = query_states.dtype
         q = query_states.squeeze(2)

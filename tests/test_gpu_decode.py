@@ -288,6 +288,24 @@ def test_hf_adapter(dev):
     close(out_w, ref_w, **F16_TOL)
 
 
+def test_hf_adapters_head_dim_64(dev):
+    # a head-dim-64 model through both HF adapters: the 16-bit kernel runs it,
+    # the FP8 adapter included (e4m3 KV is served at head dim 128 only)
+    class M:
+        num_key_value_heads = 8
+    lens_pos = torch.tensor([700], device=dev)
+    B, S = 2, 1024
+    qs = torch.randn(B, 64, 1, 64, device=dev, dtype=torch.bfloat16)
+    ks = torch.randn(B, 8, S, 64, device=dev, dtype=torch.bfloat16)
+    vs = torch.randn(B, 8, S, 64, device=dev, dtype=torch.bfloat16)
+    ref = O.decode_dense(qs.squeeze(2).float().cpu().numpy(), ks.float().cpu().numpy(), vs.float().cpu().numpy(),
+                         [701, 701])
+    for fn in (fk.custom_hf_decode_attention_forward, fk.custom_hf_decode_attention_forward_fp8):
+        out, w = fn(M(), qs, ks, vs, None, 64 ** -0.5, past_key_values=object(), cache_position=lens_pos)
+        assert w is None and out.shape == (B, 64, 64)
+        close(out, ref, **BF16_TOL)
+
+
 # ------------------------------------------------- full BASELINE sizes
 def test_config2_full_size(dev):
     lens = W.config_lengths(2)
