@@ -64,9 +64,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-template <int KV, int HP, int D>
+template <int KV, int HP, int D, bool CP>
 constexpr size_t smem_bytes() {
-  using C = KvCfg<KV, D>;
+  using C = KvCfg<KV, D, CP>;
   return 1024 + C::STAGES * (C::STAGE_BYTES + sizeof(Meta) + sizeof(uint32_t) * HP * GPAD * 64 + 2 * sizeof(uint64_t)) +
          C::NSLOT * (sizeof(EpiSlot) + sizeof(Meta) + 2 * sizeof(uint64_t));
 }
@@ -104,28 +104,28 @@ inline uint32_t box_heads(int kv_heads, int qc) {
   return static_cast<uint32_t>((qc > 1) ? 1 : hp);
 }
 
-template <int KV, int LAYOUT, int HP, int D>
+template <int KV, int LAYOUT, int HP, int D, bool CP>
 int prepare_kernel(int device) {
   static bool done[64] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lk(mu);
   if (device < 0 || device >= 64) return fail(FK_ERR_INVALID_ARG, "device index %d out of range", device);
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP, D>,
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP, D, CP>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_bytes<KV, HP, D>()));
+                                         static_cast<int>(smem_bytes<KV, HP, D, CP>()));
     if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done[device] = true;
   }
   return FK_OK;
 }
 
-template <int KV, int HP, int D>
+template <int KV, int HP, int D, bool CP>
 int occupancy(int device, int* per_sm) {
-  int rc = prepare_kernel<KV, VARLEN, HP, D>(device);
+  int rc = prepare_kernel<KV, VARLEN, HP, D, CP>(device);
   if (rc != FK_OK) return rc;
-  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, decode_split_kernel<KV, VARLEN, HP, D>,
-                                                                      THREADS, smem_bytes<KV, HP, D>());
+  const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      per_sm, decode_split_kernel<KV, VARLEN, HP, D, CP>, THREADS, smem_bytes<KV, HP, D, CP>());
   return e == cudaSuccess ? FK_OK : fail(FK_ERR_CUDA, "occupancy query failed: %s", cudaGetErrorString(e));
 }
 
@@ -134,42 +134,42 @@ int occupancy(int device, int* per_sm) {
 // depend on the layout (the layout instantiations share shared-memory
 // footprint and launch bounds), so paged, dense and varlen calls plan
 // identical segments.
-int num_work_ctas(int device, int kv, int hp, int d = HEAD_DIM) {
-  static int cache[64][3][2][2] = {};
+int num_work_ctas(int device, int kv, int hp, int d = HEAD_DIM, bool cp = false) {
+  static int cache[64][3][2][2][2] = {};
   static std::mutex mu;
-  if (device < 0 || device >= 64 || kv < 0 || kv > 2 || hp < 1 || hp > 2) return 0;
+  if (device < 0 || device >= 64 || kv < 0 || kv > 2 || hp < 1 || hp > 2 || (cp && hp != 2)) return 0;
   if (d != 128 && (d != 64 || kv == FK_DTYPE_E4M3)) return 0;
-  const int di = d == 64 ? 0 : 1;
+  const int di = d == 64 ? 0 : 1, ci = cp ? 1 : 0;
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (cache[device][kv][hp - 1][di] > 0) return cache[device][kv][hp - 1][di];
+    if (cache[device][kv][hp - 1][di][ci] > 0) return cache[device][kv][hp - 1][di][ci];
   }
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
   int per_sm = 0, prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
-#define FK_OCC(KVT, H, DD) occupancy<KVT, H, DD>(device, &per_sm)
-#define FK_OCC16(KVT) \
-  (d == 64 ? (hp == 2 ? FK_OCC(KVT, 2, 64) : FK_OCC(KVT, 1, 64)) : (hp == 2 ? FK_OCC(KVT, 2, 128) : FK_OCC(KVT, 1, 128)))
+#define FK_OCC(KVT, H, DD, CC) occupancy<KVT, H, DD, CC>(device, &per_sm)
+#define FK_OCC_D(KVT, DD) (cp ? FK_OCC(KVT, 2, DD, true) : hp == 2 ? FK_OCC(KVT, 2, DD, false) : FK_OCC(KVT, 1, DD, false))
   int rc;
-  if (kv == FK_DTYPE_F16) rc = FK_OCC16(FK_DTYPE_F16);
-  else if (kv == FK_DTYPE_BF16) rc = FK_OCC16(FK_DTYPE_BF16);
-  else rc = hp == 2 ? FK_OCC(FK_DTYPE_E4M3, 2, 128) : FK_OCC(FK_DTYPE_E4M3, 1, 128);
-#undef FK_OCC16
+  if (kv == FK_DTYPE_F16) rc = d == 64 ? FK_OCC_D(FK_DTYPE_F16, 64) : FK_OCC_D(FK_DTYPE_F16, 128);
+  else if (kv == FK_DTYPE_BF16) rc = d == 64 ? FK_OCC_D(FK_DTYPE_BF16, 64) : FK_OCC_D(FK_DTYPE_BF16, 128);
+  else rc = FK_OCC_D(FK_DTYPE_E4M3, 128);
+#undef FK_OCC_D
 #undef FK_OCC
   if (prev != device) cudaSetDevice(prev);
   if (rc != FK_OK || per_sm <= 0) return 0;
   std::lock_guard<std::mutex> lk(mu);
-  cache[device][kv][hp - 1][di] = sms * per_sm;
-  return cache[device][kv][hp - 1][di];
+  cache[device][kv][hp - 1][di][ci] = sms * per_sm;
+  return cache[device][kv][hp - 1][di][ci];
 }
 
 // Grid size a workspace must be planned for: the largest over the head dims
-// the KV type supports (the workspace size functions do not take the head dim).
-int num_work_ctas_any_d(int device, int kv, int hp) {
-  const int s128 = num_work_ctas(device, kv, hp, 128);
-  const int s64 = (kv == FK_DTYPE_E4M3) ? 0 : num_work_ctas(device, kv, hp, 64);
+// the KV type supports (the workspace size functions do not take the head
+// dim), with chunk pairs when the group needs them.
+int num_work_ctas_any_d(int device, int kv, int hp, bool cp) {
+  const int s128 = num_work_ctas(device, kv, hp, 128, cp);
+  const int s64 = (kv == FK_DTYPE_E4M3) ? 0 : num_work_ctas(device, kv, hp, 64, cp);
   return (s128 <= 0 || (kv != FK_DTYPE_E4M3 && s64 <= 0)) ? 0 : (s128 > s64 ? s128 : s64);
 }
 
@@ -279,21 +279,21 @@ bool pdl_safe(const Params& p, cudaStream_t stream) {
   return safe;
 }
 
-template <int KV, int LAYOUT, int HP, int D>
+template <int KV, int LAYOUT, int HP, int D, bool CP>
 int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
-  const int rc = prepare_kernel<KV, LAYOUT, HP, D>(device);
+  const int rc = prepare_kernel<KV, LAYOUT, HP, D, CP>(device);
   if (rc != FK_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S);
   cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = smem_bytes<KV, HP, D>();
+  cfg.dynamicSmemBytes = smem_bytes<KV, HP, D, CP>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = (pdl_enabled() && pdl_safe(p, stream)) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP, D>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP, D, CP>, p);
   if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaLaunchKernelEx: %s", cudaGetErrorString(e));
   return FK_OK;
 }
@@ -301,7 +301,8 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
 template <int LAYOUT>
 int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) {
   const int hp = hp_for(p.kv_heads, p.qc);
-  const int S = num_work_ctas(device, kv, hp, p.head_dim);
+  const bool cp = hp == 2 && p.qc > 1;  // chunk pairs
+  const int S = num_work_ctas(device, kv, hp, p.head_dim, cp);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   p.num_ctas = S;
   const int kvq = p.kv_heads * p.qc;  // (KV head, query chunk) pairs per sequence
@@ -317,14 +318,13 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
   prof_mark(0, stream);
-#define FK_L(KVT, H, DD) launch_one<KVT, LAYOUT, H, DD>(p, S, device, stream)
-#define FK_L16(KVT) \
-  (p.head_dim == 64 ? (hp == 2 ? FK_L(KVT, 2, 64) : FK_L(KVT, 1, 64)) : (hp == 2 ? FK_L(KVT, 2, 128) : FK_L(KVT, 1, 128)))
+#define FK_L(KVT, H, DD, CC) launch_one<KVT, LAYOUT, H, DD, CC>(p, S, device, stream)
+#define FK_L_D(KVT, DD) (cp ? FK_L(KVT, 2, DD, true) : hp == 2 ? FK_L(KVT, 2, DD, false) : FK_L(KVT, 1, DD, false))
   int rc;
-  if (kv == FK_DTYPE_F16) rc = FK_L16(FK_DTYPE_F16);
-  else if (kv == FK_DTYPE_BF16) rc = FK_L16(FK_DTYPE_BF16);
-  else rc = hp == 2 ? FK_L(FK_DTYPE_E4M3, 2, 128) : FK_L(FK_DTYPE_E4M3, 1, 128);
-#undef FK_L16
+  if (kv == FK_DTYPE_F16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_F16, 64) : FK_L_D(FK_DTYPE_F16, 128);
+  else if (kv == FK_DTYPE_BF16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_BF16, 64) : FK_L_D(FK_DTYPE_BF16, 128);
+  else rc = FK_L_D(FK_DTYPE_E4M3, 128);
+#undef FK_L_D
 #undef FK_L
   if (rc == FK_OK) {
     prof_mark(1, stream);
@@ -388,7 +388,8 @@ extern "C" size_t fk_decode_workspace_bytes_gqa(int device, int batch, int q_hea
     return 0;
   }
   const int qc = qc_for(q_heads, kv_heads);
-  const int S = num_work_ctas_any_d(device, kv_dtype, hp_for(kv_heads, qc));
+  const int hp = hp_for(kv_heads, qc);
+  const int S = num_work_ctas_any_d(device, kv_dtype, hp, hp == 2 && qc > 1);
   if (S <= 0) {
     fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
     return 0;
@@ -654,7 +655,8 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
   if (q_heads <= 0 || q_heads % kv_heads != 0)
     return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a positive multiple of kv_heads (%d)", q_heads, kv_heads);
   const int qc = qc_for(q_heads, kv_heads);
-  const int S = num_work_ctas_any_d(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp_for(kv_heads, qc));
+  const int hp = hp_for(kv_heads, qc);
+  const int S = num_work_ctas_any_d(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp, hp == 2 && qc > 1);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   const size_t need = WsLayout::min_bytes(batch, kv_heads * qc, S);
   if (need > NOALLOC_SCRATCH_BYTES)

@@ -66,7 +66,10 @@ enum Layout { VARLEN = 0, DENSE = 1, PAGED = 2 };
 enum Flags { F_FIRST = 1, F_LAST = 2, F_WHOLE = 4, F_END = 8 };
 
 // Per KV element type and head dim D (128; 64 for 16-bit KV).
-template <int KV, int D>
+// Per KV element type, head dim D and chunk-pair mode CP (groups of more
+// than 8 query heads: the item's two head slots are two query chunks of one
+// KV head, so a stage holds that one head's tile).
+template <int KV, int D, bool CP = false>
 struct KvCfg {
   static constexpr bool FP8 = (KV == FK_DTYPE_E4M3);
   static constexpr bool BF16 = (KV == FK_DTYPE_BF16);
@@ -78,12 +81,15 @@ struct KvCfg {
   // carries as many bytes as at D = 128; each consumer warp then takes
   // TILE / 64 blocks of 16 rows.
   static constexpr int TILE = (D == 64) ? 128 : 64;
-  static constexpr int TILE_BYTES = TILE * D * ES;           // K (or V) bytes per stage
-  static constexpr int PAGE_BYTES = PAGE * D * ES;           // one page of K (or V)
-  static constexpr int STAGES = FP8 ? 4 : 5;
-  static constexpr int NSLOT = FP8 ? 1 : 2;                  // epilogue slots (smem budget: 2 CTAs/SM for FP8)
+  static constexpr int HPL = CP ? 1 : 2;                     // KV heads laid out per stage (at most)
+  static constexpr int TILE_BYTES = TILE / 2 * HPL * D * ES; // K (or V) bytes per stage
+  static constexpr int PAGE_BYTES = PAGE * D * ES;           // one page of one head's K (or V)
+  // Chunk pairs do twice the MMA and softmax work per byte: their smaller
+  // stages let two CTAs share an SM (16-bit) or keep more stages (e4m3).
+  static constexpr int STAGES = FP8 ? (CP ? 6 : 4) : (CP ? 4 : 5);
+  static constexpr int NSLOT = (FP8 || CP) ? 1 : 2;          // epilogue slots (shared-memory budget)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  static constexpr int MINB = FP8 ? 2 : 1;                   // resident CTAs per SM (at least)
+  static constexpr int MINB = (FP8 || CP) ? 2 : 1;           // resident CTAs per SM (at least)
 };
 
 // One epilogue slot: the four consumer warps' online-softmax states of a
@@ -103,14 +109,15 @@ struct EpiSlot {
 // Row r of head hh, 16-byte chunk c is at row_off(hh, r) + (c >> 3) *
 // HALF_STRIDE + (((c & 7) ^ (r & 7)) << 4).  All bases are multiples of 1024
 // bytes, so the swizzle line of row r is r & 7 everywhere.
-template <int KV, int LAYOUT, int HP, int D>
+template <int KV, int LAYOUT, int HP, int D, bool CP = false>
 struct TileLayout {
   static constexpr bool PG = LAYOUT == 2;  // PAGED
-  static constexpr int NH = KvCfg<KV, D>::NH;
-  static constexpr int TT = KvCfg<KV, D>::TILE / HP;
+  static constexpr int NH = KvCfg<KV, D, CP>::NH;
+  static constexpr int TT = KvCfg<KV, D, CP>::TILE / HP;
+  static constexpr int HS = CP ? 1 : HP;   // KV heads stored per stage
   static constexpr uint32_t HALF_STRIDE = PG ? 2048u : uint32_t(TT * 128);
   __device__ static __forceinline__ uint32_t row_off(int hh, int r) {
-    if constexpr (PG) return uint32_t((r >> 4) * (HP * NH * 2048) + hh * (NH * 2048) + (r & 15) * 128);
+    if constexpr (PG) return uint32_t((r >> 4) * (HS * NH * 2048) + hh * (NH * 2048) + (r & 15) * 128);
     else return uint32_t(hh * (NH * TT * 128) + r * 128);
   }
 };
@@ -191,10 +198,6 @@ struct Params {
 // chunk is an item.  Slot hh holds query heads item_q(hi, hh, j) of KV head
 // item_kv(hi), j < item_g(hi, hh) (0 for the empty second slot of an odd
 // chunk count).
-template <int HP>
-__device__ __forceinline__ bool chunk_pairs(const Params& p) {
-  return HP == 2 && p.qc > 1;
-}
 template <int HP>
 __device__ __forceinline__ int item_kv(const Params& p, int hi) {
   if (p.qc == 1) return hi * HP;
@@ -321,10 +324,11 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // ------------------------------------------------------------------------
 // Split pass.
 // ------------------------------------------------------------------------
-template <int KV, int LAYOUT, int HP, int D>
-__global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
-  using C = KvCfg<KV, D>;
-  using TL = TileLayout<KV, LAYOUT, HP, D>;
+template <int KV, int LAYOUT, int HP, int D, bool CP>
+__global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
+  static_assert(!CP || HP == 2, "chunk pairs fill the two head slots of an item");
+  using C = KvCfg<KV, D, CP>;
+  using TL = TileLayout<KV, LAYOUT, HP, D, CP>;
   constexpr int KD = C::KD;
   constexpr int TT = C::TILE / HP;       // tokens per KV head in one stage
   constexpr int WPH = CWARPS / HP;       // consumer warps per KV head
@@ -380,7 +384,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
   // zeroed once, here.  Otherwise the producer converts Q through registers.
   const bool q_async = p.q_al16 && p.q_dtype == (C::BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16);
   // fewest query heads in a slot of any item
-  const int gmin = p.qc == 1 ? p.G : (chunk_pairs<HP>(p) && (p.qc & 1)) ? 0 : (p.G % 8 == 0 ? 8 : p.G % 8);
+  const int gmin = p.qc == 1 ? p.G : (CP && (p.qc & 1)) ? 0 : (p.G % 8 == 0 ? 8 : p.G % 8);
   if (q_async && gmin < GPAD) {
     const int npad = GPAD - gmin;
     for (int u = threadIdx.x; u < C::STAGES * HP * npad * 16; u += THREADS) {
@@ -554,9 +558,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
           const uint32_t sV = sK + C::TILE_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
           int bad = 0;
-          // chunk pairs load one KV head: half a stage
-          const uint32_t nkv = chunk_pairs<HP>(p) ? 1u : static_cast<uint32_t>(HP);
-          uint32_t bytes = 2u * C::TILE_BYTES / HP * nkv;
+          // chunk pairs load one KV head
+          constexpr uint32_t nkv = CP ? 1u : static_cast<uint32_t>(HP);
+          uint32_t bytes = 2u * C::TILE_BYTES;
           int phys = -1;
           if constexpr (LAYOUT == PAGED) {
             const int p0 = tt / PAGE;
@@ -634,7 +638,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
           if constexpr (LAYOUT == PAGED) {
             if (phys >= 0) {
               // one box per page: 16 tokens x HP heads x D dims
-              const uint32_t off = lane * (HP * C::PAGE_BYTES);
+              const uint32_t off = lane * (nkv * C::PAGE_BYTES);
               if constexpr (C::FP8) {
                 tma_load_4d(sK + off, &p.tk, fb, 0, 0, hcoord, phys);
                 tma_load_4d(sV + off, &p.tv, fb, 0, 0, hcoord, phys);
@@ -880,7 +884,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D>::MINB) decode_split_kern
   const int g = lane >> 2;
   const int t = lane & 3;
   const int hh = warp / WPH;            // head slot of the item this warp serves
-  const int hk = chunk_pairs<HP>(p) ? 0 : hh;  // its KV head's tile in the stage
+  const int hk = CP ? 0 : hh;            // its KV head's tile in the stage
   const int r0 = (warp % WPH) * 16;      // its 16 rows of that head's tile
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(D)) * LOG2E * sk;
