@@ -112,24 +112,30 @@ def setup_workload(name, rank, world, device):
     with a zero-arg `run()` (one decode step through the public API), the
     per-step inputs for the e2e leg, algorithmic KV bytes and a config dict."""
     import fasterkernels_b200 as fk
-    if name in ("config2", "config2s"):
+    if name in ("config2", "config2s", "config2g16", "config2d64"):
+        # config2g16 / config2d64: config 2's lengths with a 16-head GQA group
+        # (128 query heads) / with head dim 64 (64 query heads), shapes the
+        # reference's Triton kernels take beyond BASELINE's configs
         spec = W.CONFIGS[2]
         lens = W.config_lengths(2, seed=0)
         if name == "config2s":  # profiling case: first 8 sequences (~0.4 GB of KV, still > L2)
             lens = lens[:8]
-        d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, device, seed=rank, sinks=True)
+        qh = {"config2g16": 128, "config2d64": 64}.get(name, spec.q_heads)
+        hd = 64 if name == "config2d64" else 128
+        d = W.make_varlen(lens, qh, spec.kv_heads, torch.float16, device, seed=rank, sinks=True, head_dim=hd)
         q, k, v, cu, s = d["q"], d["k"], d["v"], d["cu_seqlens"], d["s_aux"]
         out = torch.empty_like(q)
 
         def run(qq=q, cc=cu, oo=out):
             return fk.flash_decode_gqa_varlen(qq, k, v, cc, s, out=oo)
-        kvb = W.kv_bytes(lens, spec.kv_heads, 2)
-        cfg = {"workload": spec.name + ("" if name == "config2" else "_first8"), "batch_per_gpu": len(lens),
+        kvb = W.kv_bytes(lens, spec.kv_heads, 2, hd)
+        suffix = {"config2": "", "config2s": "_first8", "config2g16": "_g16", "config2d64": "_d64"}[name]
+        cfg = {"workload": spec.name + suffix, "batch_per_gpu": len(lens),
                "global_batch": len(lens) * world,
-               "q_heads": spec.q_heads, "kv_heads": spec.kv_heads, "head_dim": 128,
+               "q_heads": qh, "kv_heads": spec.kv_heads, "head_dim": hd,
                "seq_lens": "U[8192,16384] seed 0 (same per-GPU work on every rank; q/k/v/s_aux seed = rank)", "tokens_this_rank": int(sum(lens)),
                "kv_layout": "contiguous varlen [T, KV_H, D] fp16", "sinks": True,
-               "l2": "inputs larger than L2 (>=1.5 GB KV per GPU, no flush)",
+               "l2": "inputs larger than L2 (>=0.77 GB KV per GPU, no flush)",
                "parallelism": f"dp{world} (each rank its own batch, no collective)"}
         return dict(run=run, q=q, lens_dev=cu, out=out, kv_bytes=kvb, cfg=cfg, scaling="weak",
                     sample=(q, k, v, cu, s, lens), dtype="fp16 in / fp32 accumulate")
@@ -410,15 +416,16 @@ def run_reference(args, rank, world):
     else:
         spec = W.CONFIGS[2]
         lens = W.config_lengths(2, seed=0)
-        kvh, qh, es = spec.kv_heads, spec.q_heads, 2
+        kvh, qh, es = spec.kv_heads, {"config2g16": 128, "config2d64": 64}.get(args.workload, spec.q_heads), 2
+    hd = 64 if args.workload == "config2d64" else 128
     L = lens[0]
     g = torch.Generator().manual_seed(0)
-    q = torch.randn(1, qh, 128, generator=g).numpy()
-    k = torch.randn(L, kvh, 128, generator=g).half().numpy()
-    v = torch.randn(L, kvh, 128, generator=g).half().numpy()
+    q = torch.randn(1, qh, hd, generator=g).numpy()
+    k = torch.randn(L, kvh, hd, generator=g).half().numpy()
+    v = torch.randn(L, kvh, hd, generator=g).half().numpy()
     s = torch.randn(qh, generator=g).numpy()
     cu = np.array([0, L])
-    byt = W.kv_bytes([L], kvh, es)
+    byt = W.kv_bytes([L], kvh, es, hd)
     for _ in range(args.warmup):
         O.decode_varlen(q, k, v, cu, s, dtype=np.float32)
     t0 = time.perf_counter()
@@ -432,7 +439,8 @@ def run_reference(args, rank, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "strong" if args.workload == "config5" else "weak",
             "vs_baseline": None, "dtype": "fp32 (CPU)", "data": "synthetic",
-            "config": {"workload": spec.name, "sample": desc},
+            "config": {"workload": spec.name + {"config2g16": "_g16", "config2d64": "_d64"}.get(args.workload, ""),
+                       "sample": desc},
             "cpu_baseline": {"value": round(val, 6), "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
             "e2e": {"value": round(val, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -443,7 +451,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["config2", "config2s", "config3", "config3v", "config4", "config4d", "config5"], default="config2")
+    ap.add_argument("--workload", choices=["config2", "config2s", "config2g16", "config2d64", "config3", "config3v", "config4",
+                                           "config4d", "config5"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

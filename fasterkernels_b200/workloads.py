@@ -61,9 +61,9 @@ def config_lengths(cfg: int | ConfigSpec, seed: int = 0) -> list[int]:
     return [int(round(math.exp(float(x) * math.log(hi / lo) + math.log(lo)))) for x in u]
 
 
-def kv_bytes(lens, kv_heads: int, elem_bytes: int) -> int:
+def kv_bytes(lens, kv_heads: int, elem_bytes: int, head_dim: int = D) -> int:
     """Algorithmic bytes of one decode step: K and V of the valid tokens."""
-    return int(sum(lens)) * kv_heads * D * 2 * elem_bytes
+    return int(sum(lens)) * kv_heads * head_dim * 2 * elem_bytes
 
 
 def _gen(device, seed):
