@@ -104,14 +104,14 @@ inline uint32_t box_heads(int kv_heads, int qc) {
   return static_cast<uint32_t>((qc > 1) ? 1 : hp);
 }
 
-template <int KV, int LAYOUT, int HP, int D, bool CP>
+template <int KV, int LAYOUT, int HP, int D, bool CP, bool QC>
 int prepare_kernel(int device) {
   static bool done[64] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lk(mu);
   if (device < 0 || device >= 64) return fail(FK_ERR_INVALID_ARG, "device index %d out of range", device);
   if (!done[device]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP, D, CP>,
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<KV, LAYOUT, HP, D, CP, QC>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem_bytes<KV, HP, D, CP>()));
     if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -122,10 +122,10 @@ int prepare_kernel(int device) {
 
 template <int KV, int HP, int D, bool CP>
 int occupancy(int device, int* per_sm) {
-  int rc = prepare_kernel<KV, VARLEN, HP, D, CP>(device);
+  int rc = prepare_kernel<KV, VARLEN, HP, D, CP, false>(device);
   if (rc != FK_OK) return rc;
   const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      per_sm, decode_split_kernel<KV, VARLEN, HP, D, CP>, THREADS, smem_bytes<KV, HP, D, CP>());
+      per_sm, decode_split_kernel<KV, VARLEN, HP, D, CP, false>, THREADS, smem_bytes<KV, HP, D, CP>());
   return e == cudaSuccess ? FK_OK : fail(FK_ERR_CUDA, "occupancy query failed: %s", cudaGetErrorString(e));
 }
 
@@ -279,9 +279,9 @@ bool pdl_safe(const Params& p, cudaStream_t stream) {
   return safe;
 }
 
-template <int KV, int LAYOUT, int HP, int D, bool CP>
+template <int KV, int LAYOUT, int HP, int D, bool CP, bool QC>
 int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
-  const int rc = prepare_kernel<KV, LAYOUT, HP, D, CP>(device);
+  const int rc = prepare_kernel<KV, LAYOUT, HP, D, CP, QC>(device);
   if (rc != FK_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S);
@@ -293,7 +293,7 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = (pdl_enabled() && pdl_safe(p, stream)) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP, D, CP>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP, D, CP, QC>, p);
   if (e != cudaSuccess) return fail(FK_ERR_CUDA, "cudaLaunchKernelEx: %s", cudaGetErrorString(e));
   return FK_OK;
 }
@@ -318,12 +318,15 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
   prof_mark(0, stream);
-#define FK_L(KVT, H, DD, CC) launch_one<KVT, LAYOUT, H, DD, CC>(p, S, device, stream)
-#define FK_L_D(KVT, DD) (cp ? FK_L(KVT, 2, DD, true) : hp == 2 ? FK_L(KVT, 2, DD, false) : FK_L(KVT, 1, DD, false))
+  // e4m3 KV with bf16 or e4m3 Q copied raw: the consumers convert it
+  const bool qconv = kv == FK_DTYPE_E4M3 && p.q_al16 && p.q_dtype != FK_DTYPE_F16;
+#define FK_L(KVT, H, DD, CC, QQ) launch_one<KVT, LAYOUT, H, DD, CC, QQ>(p, S, device, stream)
+#define FK_L_D(KVT, DD, QQ) \
+  (cp ? FK_L(KVT, 2, DD, true, QQ) : hp == 2 ? FK_L(KVT, 2, DD, false, QQ) : FK_L(KVT, 1, DD, false, QQ))
   int rc;
-  if (kv == FK_DTYPE_F16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_F16, 64) : FK_L_D(FK_DTYPE_F16, 128);
-  else if (kv == FK_DTYPE_BF16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_BF16, 64) : FK_L_D(FK_DTYPE_BF16, 128);
-  else rc = FK_L_D(FK_DTYPE_E4M3, 128);
+  if (kv == FK_DTYPE_F16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_F16, 64, false) : FK_L_D(FK_DTYPE_F16, 128, false);
+  else if (kv == FK_DTYPE_BF16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_BF16, 64, false) : FK_L_D(FK_DTYPE_BF16, 128, false);
+  else rc = qconv ? FK_L_D(FK_DTYPE_E4M3, 128, true) : FK_L_D(FK_DTYPE_E4M3, 128, false);
 #undef FK_L_D
 #undef FK_L
   if (rc == FK_OK) {
@@ -365,10 +368,8 @@ void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out
   p.scale_v = scale_v;
   p.ws = static_cast<unsigned char*>(ws);
   p.qc = qc_for(q_heads, kv_heads);
-  p.q_al16 = (q_dtype != FK_DTYPE_E4M3 && (reinterpret_cast<uintptr_t>(q) & 15) == 0 && (sq_b & 7) == 0 &&
-              (sq_h & 7) == 0)
-                 ? 1
-                 : 0;
+  const int64_t qes = (q_dtype == FK_DTYPE_E4M3) ? 1 : 2;
+  p.q_al16 = ((reinterpret_cast<uintptr_t>(q) & 15) == 0 && ((sq_b * qes) & 15) == 0 && ((sq_h * qes) & 15) == 0) ? 1 : 0;
 }
 
 }  // namespace fk

@@ -324,9 +324,13 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // ------------------------------------------------------------------------
 // Split pass.
 // ------------------------------------------------------------------------
-template <int KV, int LAYOUT, int HP, int D, bool CP>
+// QC: the consumers convert Q staged raw (bf16 or e4m3 Q over e4m3 KV) to the
+// MMA type as they load it; its own instantiation keeps that code out of the
+// kernels that never need it.
+template <int KV, int LAYOUT, int HP, int D, bool CP, bool QC>
 __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
   static_assert(!CP || HP == 2, "chunk pairs fill the two head slots of an item");
+  static_assert(!QC || KV == FK_DTYPE_E4M3, "16-bit KV takes Q of its own type");
   using C = KvCfg<KV, D, CP>;
   using TL = TileLayout<KV, LAYOUT, HP, D, CP>;
   constexpr int KD = C::KD;
@@ -378,11 +382,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
     }
     fence_mbar_init();
   }
-  // Q already of the MMA type and 16-byte aligned: each segment's Q rows are
-  // copied straight into the stage's Q slot by cp.async, completing on the
-  // stage's full barrier with the KV tiles; the padding rows (heads G..7) are
-  // zeroed once, here.  Otherwise the producer converts Q through registers.
-  const bool q_async = p.q_al16 && p.q_dtype == (C::BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16);
+  // Q rows 16-byte aligned: each segment's Q rows are copied raw into the
+  // stage's Q slot by cp.async, completing on the stage's full barrier with
+  // the KV tiles, and the consumers convert them to the MMA type (and apply
+  // scale_q) as they load them; the padding rows (heads G..7) are zeroed
+  // once, here.  Otherwise the producer converts Q through registers.
+  const bool q_async = p.q_al16 != 0;
   // fewest query heads in a slot of any item
   const int gmin = p.qc == 1 ? p.G : (CP && (p.qc & 1)) ? 0 : (p.G % 8 == 0 ? 8 : p.G % 8);
   if (q_async && gmin < GPAD) {
@@ -595,13 +600,16 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
               // 256-byte row slots
               const uint32_t qd = smem_u32(qs);
               const long long qb0 = static_cast<long long>(b) * p.q_sb;
+              const int qes = (p.q_dtype == FK_DTYPE_E4M3) ? 1 : 2;  // Q bytes per element
+              const int nch = D * qes / 16;                          // 16-byte copies per row
               const int g0 = item_g<HP>(p, hi, 0), g1 = HP == 2 ? item_g<HP>(p, hi, 1) : 0;
-              for (int u = lane; u < (g0 + g1) * (D / 8); u += 32) {
-                const int r = u / (D / 8), c = u % (D / 8);
+              for (int u = lane; u < (g0 + g1) * nch; u += 32) {
+                const int r = u / nch, c = u % nch;
                 const int hh = r < g0 ? 0 : 1, j = r < g0 ? r : r - g0;
                 const int qh = item_q<HP>(p, hi, hh, j);
                 cp_async16(qd + (hh * GPAD + j) * 256 + c * 16,
-                           static_cast<const unsigned short*>(p.q) + qb0 + static_cast<long long>(qh) * p.q_sh + c * 8);
+                           static_cast<const unsigned char*>(p.q) +
+                               (qb0 + static_cast<long long>(qh) * p.q_sh) * qes + c * 16);
               }
               cp_async_mbar_arrive(fb);
             } else {
@@ -887,6 +895,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
   const int hk = CP ? 0 : hh;            // its KV head's tile in the stage
   const int r0 = (warp % WPH) * 16;      // its 16 rows of that head's tile
   const float sk = (p.scale_k != nullptr) ? __ldg(p.scale_k) : 1.f;
+  // Q staged raw by cp.async but not of the MMA type: convert on load
+  const float qscale = (QC && p.scale_q != nullptr) ? __ldg(p.scale_q) : 1.f;
   const float qk_scale = rsqrtf(static_cast<float>(D)) * LOG2E * sk;
 
   float m[2], l[2], acc[KD][4];
@@ -938,8 +948,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       l[0] = l[1] = 0.f;
 #pragma unroll
       for (int i = 0; i < KD; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-      // the producer staged this item's Q rows (MMA type, zero-padded to 8
-      // heads) next to the segment's first tile
+      // the producer staged this item's Q rows (zero-padded to 8 heads) next
+      // to the segment's first tile: raw rows (cp.async) or MMA-type pairs
       const uint32_t* qrow = qstage + stage * QWORDS + hh * (GPAD * 64) + g * 64;
 #pragma unroll
       for (int j = 0; j < KD; ++j) {
@@ -951,8 +961,17 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           d0 = 16 * j + 2 * t;
           d1 = d0 + 8;
         }
-        qb[j][0] = qrow[d0 >> 1];
-        qb[j][1] = qrow[d1 >> 1];
+        if constexpr (!QC) {
+          qb[j][0] = qrow[d0 >> 1];
+          qb[j][1] = qrow[d1 >> 1];
+        } else if (p.q_dtype == FK_DTYPE_E4M3) {  // raw bytes: pair (d, d+1) at byte d
+          const unsigned char* qbytes = reinterpret_cast<const unsigned char*>(qrow);
+          qb[j][0] = q_pair_to_mma<MBF16>(p, *reinterpret_cast<const unsigned short*>(qbytes + d0), qscale);
+          qb[j][1] = q_pair_to_mma<MBF16>(p, *reinterpret_cast<const unsigned short*>(qbytes + d1), qscale);
+        } else {  // raw 16-bit pairs of the other 16-bit type
+          qb[j][0] = q_pair_to_mma<MBF16>(p, qrow[d0 >> 1], qscale);
+          qb[j][1] = q_pair_to_mma<MBF16>(p, qrow[d1 >> 1], qscale);
+        }
       }
     }
 
