@@ -701,3 +701,30 @@ def test_head_dim_64_append_then_decode(dev):
         fk.paged_flash_decode(torch.zeros(B, 32, 64, device=dev, dtype=torch.float16), kp.view(torch.uint8)[..., :64]
                               .view(torch.float8_e4m3fn), kp.view(torch.uint8)[..., :64].view(torch.float8_e4m3fn),
                               bt, pos, 16)
+
+
+def test_fp8_query_paged_raw_copy_matches_register_path(dev):
+    # an e4m3 query with scale_q, as the reference's FP8 entry takes it: rows
+    # aligned to 16 bytes are copied raw and converted by the consumers; an
+    # unaligned strided view goes through the producer's registers.  Same
+    # formula, so the outputs are bit-identical.
+    lens = [1, 33, 1500, 0, 4097, 777]
+    d = W.make_varlen(lens, 32, 8, torch.float32, dev, seed=77, sinks=True)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    q8, sq = fk.quantize_to_fp8(d["q"])
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=4)
+    kp, vp = kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    out = fk.paged_flash_decode(q8, kp, vp, bt, sl, 16, s_aux=d["s_aux"], scale_q=sq, scale_k=sk, scale_v=sv,
+                                out_dtype=torch.float16)
+    qbig = torch.zeros(len(lens), 32, 136, dtype=torch.uint8, device=dev)
+    qbig[:, :, :128] = q8.view(torch.uint8)
+    qv = qbig.view(torch.float8_e4m3fn)[:, :, :128]  # head stride 136 bytes: not 16-byte aligned
+    out_v = fk.paged_flash_decode(qv, kp, vp, bt, sl, 16, s_aux=d["s_aux"], scale_q=sq, scale_k=sk, scale_v=sv,
+                                  out_dtype=torch.float16)
+    assert torch.equal(out, out_v)
+    qd = (q8.float() * sq).half()
+    ref = O.decode_varlen(qd.float().cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
+                          d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
+    close(out, ref, atol=3e-3, rtol=1e-2)
