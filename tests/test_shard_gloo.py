@@ -64,3 +64,52 @@ def test_kv_head_split_and_choice():
     assert shard.choose_partition(128, 8, 8) == "sequence"
     sh = shard.shard_sequences([5, 4, 3, 2, 1], 2, 0)
     assert sh.indices == [0, 3, 4] and sh.kv_tokens == 8
+
+
+def _failing_worker(rank, world, port, q, mode):
+    """Rank 1 fails before the output gather: it raises and exits ("exit"), or
+    stays alive without joining ("stall").  Rank 0 must get an error from the
+    gather within the process group's timeout instead of hanging."""
+    import datetime
+    import time
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+        lens = W.config_lengths(5)
+        sh = shard.shard_sequences(lens, world, rank)
+        out = torch.stack([torch.full((4, 8), float(i)) for i in sh.indices])
+        if rank == 1:
+            if mode == "stall":
+                time.sleep(8)
+                q.put((rank, "stalled", 0.0))
+                return
+            raise RuntimeError("simulated rank failure before the gather")
+        t0 = time.time()
+        try:
+            shard.gather_outputs(out, sh.indices, len(lens))
+            q.put((rank, "no error", time.time() - t0))
+        except Exception as e:  # the expected path: the peer is gone or late
+            q.put((rank, "error:" + type(e).__name__, time.time() - t0))
+    except Exception as e:
+        q.put((rank, "raised:" + str(e)[:60], 0.0))
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_gather_fails_fast_when_a_rank_dies(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r = q.get(timeout=120)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():  # pragma: no cover
+            p.kill()
+    assert res[0][1].startswith("error:"), res
+    assert res[0][2] < 60.0, res  # bounded by the process-group timeout, not a hang
+    assert res[1][1].startswith("raised:simulated") if mode == "exit" else res[1][1] == "stalled"
