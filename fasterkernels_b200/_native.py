@@ -93,6 +93,8 @@ def lib() -> ctypes.CDLL:
         L.fk_profile_end.argtypes = [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_I)]
         L.fk_decode_num_ctas.restype = _I
         L.fk_decode_num_ctas.argtypes = [_I, _I, _I]
+        L.fk_debug_configure.restype = _I
+        L.fk_debug_configure.argtypes = [ctypes.c_ulonglong, _I]
         _lib = L
         return L
 
@@ -177,12 +179,17 @@ def device_workspaces(device=None):
 def read_status(device=None, clear: bool = True) -> int:
     """Read (and by default clear) the sticky FK_STATUS_* word of a device's
     workspaces (OR over its streams).  Synchronises with the device; keep it
-    off the hot path."""
+    off the hot path.  After FK_STATUS_TIMEOUT the whole workspace is cleared
+    when clearing: a kernel that gave up may leave arrival counters mid-count."""
     st = 0
     for ws in device_workspaces(device):
-        st |= int(ws[:4].view(torch.int32).item())
+        w = int(ws[:4].view(torch.int32).item())
+        st |= w
         if clear:
-            ws[:4].zero_()
+            if w & FK_STATUS_TIMEOUT:
+                ws.zero_()
+            else:
+                ws[:4].zero_()
     return st
 
 

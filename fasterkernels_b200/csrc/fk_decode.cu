@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -227,6 +228,11 @@ int common_checks(const void* q, const void* k, const void* v, const void* out, 
   return FK_OK;
 }
 
+// Diagnostics set through fk_debug_configure: the bound of every mbarrier
+// wait and the stage-withholding test hook (see Params::inject).
+std::atomic<unsigned long long> g_wait_ns{4000000000ull};
+std::atomic<int> g_inject{0};
+
 // Programmatic dependent launch of consecutive decode kernels (default on;
 // FK_DECODE_PDL=0 turns it off).
 inline bool pdl_enabled() {
@@ -351,6 +357,8 @@ void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out
                  const float* scale_q, const float* scale_k, const float* scale_v, void* ws) {
   p.q = q;
   p.head_dim = head_dim;
+  p.wait_ns = g_wait_ns.load();
+  p.inject = g_inject.load();
   p.q_sb = sq_b;
   p.q_sh = sq_h;
   p.out = out;
@@ -590,6 +598,15 @@ extern "C" int fk_profile_end(float* kernel_ms, int* launches) {
   }
   if (kernel_ms) *kernel_ms = total;
   if (launches) *launches = g_prof.n;
+  return FK_OK;
+}
+
+extern "C" int fk_debug_configure(unsigned long long wait_ns, int inject) {
+  if (wait_ns < 1000000ull || wait_ns > 60000000000ull)
+    return fail(FK_ERR_INVALID_ARG, "wait_ns must be in [1 ms, 60 s]");
+  if (inject != 0 && inject != 1) return fail(FK_ERR_INVALID_ARG, "inject must be 0 or 1");
+  g_wait_ns.store(wait_ns);
+  g_inject.store(inject);
   return FK_OK;
 }
 

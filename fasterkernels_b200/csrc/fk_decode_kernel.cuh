@@ -187,6 +187,8 @@ struct Params {
   int q_al16;  // q base and strides 16-byte aligned (rows can be copied with cp.async)
   int qc;      // query chunks of at most 8 heads per KV head: ceil(G / 8)
   int head_dim;  // D (the kernel is instantiated per D; kept for host checks)
+  unsigned long long wait_ns;  // bound of every mbarrier wait
+  int inject;                  // test hook: 1 = each CTA's producer withholds its first stage
 };
 
 // Work items of a sequence and their two head slots hh < HP (an MMA N of 8
@@ -450,13 +452,18 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
     int stage = 0;
     uint32_t phase = 0;
     bool alive = true;
+    // Test hook (off unless the host sets it): publish nothing for the first
+    // stage, so the consumers' bounded wait on it runs out and the kernel
+    // returns with FK_STATUS_TIMEOUT.  Nothing is left in flight: no copy
+    // is issued for that stage.
+    bool withhold = p.inject == 1;
     // Claim the next ring slot (waits for the consumers to release it).
     auto acquire = [&]() -> bool {
       int ok = 1;
 #ifdef FK_TRACE
       const unsigned long long tq0 = gtimer();
 #endif
-      if (lane == 0) ok = mbar_wait(smem_u32(&empty[stage]), phase ^ 1u) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, p.wait_ns) ? 1 : 0;
 #ifdef FK_TRACE
       if (lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][6] += gtimer() - tq0;
 #endif
@@ -555,6 +562,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           if (!acquire()) {
             alive = false;
             break;
+          }
+          if (withhold) {
+            withhold = false;
+            advance();
+            continue;
           }
 #ifdef FK_TRACE
           const long long tc1 = clock64();
@@ -747,7 +759,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 #ifdef FK_TRACE
       const unsigned long long te0 = gtimer();
 #endif
-      if (!mbar_wait(smem_u32(&efull[eb]), eph)) {
+      if (!mbar_wait(smem_u32(&efull[eb]), eph, p.wait_ns)) {
         if (et == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
         break;
       }
@@ -920,14 +932,14 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 #ifdef FK_TRACE
     const unsigned long long tw0 = gtimer();
 #endif
-    if (!mbar_wait(smem_u32(&full[stage]), phase)) {
+    if (!mbar_wait(smem_u32(&full[stage]), phase, p.wait_ns)) {
       if (lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
       break;
     }
     const Meta mt = meta[stage];
     if (mt.flags & F_END) {
       // tell the epilogue warps to finish
-      if (mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u)) {
+      if (mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u, p.wait_ns)) {
         if (warp == 0 && lane == 0) emeta[eb].flags = F_END;
         mbar_arrive(smem_u32(&efull[eb]));
       } else if (lane == 0) {
@@ -1117,7 +1129,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 #ifdef FK_TRACE
       const unsigned long long tq = gtimer();
 #endif
-      const bool eok = mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u);
+      const bool eok = mbar_wait(smem_u32(&eempty[eb]), ephase ^ 1u, p.wait_ns);
 #ifdef FK_TRACE
       if (threadIdx.x == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][21] += gtimer() - tq;
 #endif

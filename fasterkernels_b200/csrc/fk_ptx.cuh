@@ -48,7 +48,8 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase of parity `parity` to complete.  try_wait
 // suspends the thread in hardware until the phase completes or a short
 // system-defined limit passes, so the loop wakes as soon as the phase flips;
-// it gives up after about four seconds of %globaltimer and returns false so
+// it gives up after limit_ns of %globaltimer (four seconds unless the launch
+// sets another limit) and returns false so
 // that the caller can record FK_STATUS_TIMEOUT and leave its loop instead of
 // hanging the GPU.
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -57,16 +58,14 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long limit_ns = 4000000000ull) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
 #pragma unroll 1
   while (true) {
-#ifdef FK_WAIT_SLEEP
-    __nanosleep(FK_WAIT_SLEEP);
-#endif
     if (mbar_test(bar, parity)) return true;
-    if (global_ns() - t0 > 4000000000ull) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
 }
 

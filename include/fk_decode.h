@@ -227,6 +227,17 @@ size_t fk_noalloc_scratch_bytes(void);
  * KV element type and KV head count. */
 int fk_decode_num_ctas(int device, int kv_dtype, int kv_heads);
 
+/*
+ * Diagnostics for tests of the bounded waits (no counterpart in the
+ * reference).  wait_ns bounds every mbarrier wait of later launches (default
+ * 4 s, range [1 ms, 60 s]); inject = 1 makes each CTA's producer publish
+ * nothing for its first pipeline stage, so its consumers' wait runs out, the
+ * kernel sets FK_STATUS_TIMEOUT and returns (no fault, nothing left in
+ * flight).  Clear the workspace after a timeout: arrival counters of split
+ * items may be left mid-count.  inject = 0 restores normal operation.
+ */
+int fk_debug_configure(unsigned long long wait_ns, int inject);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,6 +5,8 @@ Tolerances: fp16 output atol 2e-3 / rtol 1e-2 (fp32 accumulation); bf16
 atol 1e-2 / rtol 2e-2 (bf16 P and V operands); FP8 KV atol 2e-2 against the
 oracle on the dequantised KV; paged vs contiguous bit-identical.
 """
+import time
+
 import numpy as np
 import pytest
 import torch
@@ -728,3 +730,30 @@ def test_fp8_query_paged_raw_copy_matches_register_path(dev):
     ref = O.decode_varlen(qd.float().cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
                           d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
     close(out, ref, atol=3e-3, rtol=1e-2)
+
+
+def test_bounded_wait_runs_out_and_reports_timeout(dev):
+    # Every mbarrier wait is bounded.  With the test hook each CTA's producer
+    # publishes nothing for its first stage, so the consumers' wait on it runs
+    # out (0.2 s here); the kernel returns with FK_STATUS_TIMEOUT instead of
+    # hanging, the context stays usable, and the next call is correct.
+    q, k, v, cu, s = _rand_case(dev, [3000, 50, 9000], 32, 8, torch.float16, True, seed=90)
+    ref = _oracle(q, k, v, cu, s)
+    fk.flash_decode_gqa_varlen(q, k, v, cu, s)  # workspace exists before the hook
+    torch.cuda.synchronize()
+    assert N.read_status(dev) == 0
+    L = N.lib()
+    assert L.fk_debug_configure(200_000_000, 1) == 0
+    try:
+        t0 = time.time()
+        fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 10.0
+        assert N.read_status(dev) & N.FK_STATUS_TIMEOUT
+    finally:
+        assert L.fk_debug_configure(4_000_000_000, 0) == 0
+    out = fk.flash_decode_gqa_varlen(q, k, v, cu, s)
+    torch.cuda.synchronize()
+    close(out, ref, **F16_TOL)
+    assert N.read_status(dev) == 0
+    assert L.fk_debug_configure(10, 0) != 0  # out-of-range bound refused
