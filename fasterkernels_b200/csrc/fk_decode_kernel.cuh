@@ -361,6 +361,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
   float* ws_acc = reinterpret_cast<float*>(p.ws + p.ws_acc);
   const int KVI = items_per_seq<HP>(p);
   __shared__ int s_last;
+  __shared__ int s_eok[2][EWARPS];  // epilogue warps' wait outcomes, by iteration parity
 
 #ifdef FK_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 4096) {
@@ -755,11 +756,21 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
     const float sv = (p.scale_v != nullptr) ? __ldg(p.scale_v) : 1.f;
     int eb = 0;
     uint32_t eph = 0;
+    int it = 0;
     while (true) {
 #ifdef FK_TRACE
       const unsigned long long te0 = gtimer();
 #endif
-      if (!mbar_wait(smem_u32(&efull[eb]), eph, p.wait_ns)) {
+      // Both epilogue warps act on the same outcome of the bounded wait (one
+      // alone timing out must not leave the other in a named barrier).
+      const bool wok = mbar_wait(smem_u32(&efull[eb]), eph, p.wait_ns);
+      if (lane == 0) s_eok[it & 1][et >> 5] = wok ? 1 : 0;
+      named_bar_sync(3, ETHREADS);
+      bool eok = true;
+#pragma unroll
+      for (int w = 0; w < EWARPS; ++w) eok = eok && s_eok[it & 1][w] != 0;
+      ++it;
+      if (!eok) {
         if (et == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
         break;
       }
