@@ -100,8 +100,9 @@ struct EpiSlot {
   float cacc[CWARPS][GPAD][HEAD_DIM];
 };
 
-// Shared-memory tile layouts of one K (or V) stage: TT = 64/HP tokens of each
-// of the item's HP KV heads, 128-byte swizzled (16-byte chunk index XOR
+// Shared-memory tile layouts of one K (or V) stage: TT = TILE/HP tokens of each
+// of the item's HP KV heads (one head's with chunk pairs), 128-byte swizzled
+// (16-byte chunk index XOR
 // row & 7).  A row of D elements is NH = D * ES / 128 halves of 128 bytes
 // (16-bit D = 128: two 64-dim halves; 16-bit D = 64 and e4m3 D = 128: one).
 //   VARLEN / DENSE: [head][half][TT rows][128 B]   one TMA box per stage
