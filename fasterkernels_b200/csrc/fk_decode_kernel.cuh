@@ -102,8 +102,8 @@ struct EpiSlot {
 
 // Shared-memory tile layouts of one K (or V) stage: TT = TILE/HP tokens of each
 // of the item's HP KV heads (one head's with chunk pairs), 128-byte swizzled
-// (16-byte chunk index XOR
-// row & 7).  A row of D elements is NH = D * ES / 128 halves of 128 bytes
+// (16-byte chunk index XOR row & 7).  A row of D elements is NH = D * ES /
+// 128 halves of 128 bytes
 // (16-bit D = 128: two 64-dim halves; 16-bit D = 64 and e4m3 D = 128: one).
 //   VARLEN / DENSE: [head][half][TT rows][128 B]   one TMA box per stage
 //   PAGED:          [page][head][half][16][128 B]  one TMA box per page
