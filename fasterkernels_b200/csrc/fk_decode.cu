@@ -376,6 +376,7 @@ void fill_common(Params& p, const void* q, int64_t sq_b, int64_t sq_h, void* out
   p.scale_v = scale_v;
   p.ws = static_cast<unsigned char*>(ws);
   p.qc = qc_for(q_heads, kv_heads);
+  p.o_al8 = ((reinterpret_cast<uintptr_t>(out) & 7) == 0 && (so_b & 3) == 0 && (so_h & 3) == 0) ? 1 : 0;
   const int64_t qes = (q_dtype == FK_DTYPE_E4M3) ? 1 : 2;
   p.q_al16 = ((reinterpret_cast<uintptr_t>(q) & 15) == 0 && ((sq_b * qes) & 15) == 0 && ((sq_h * qes) & 15) == 0) ? 1 : 0;
 }

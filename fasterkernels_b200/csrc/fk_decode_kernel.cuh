@@ -186,6 +186,7 @@ struct Params {
   int q_dtype, out_dtype;
   int num_ctas;
   int q_al16;  // q base and strides 16-byte aligned (rows can be copied with cp.async)
+  int o_al8;   // out base and strides 8-byte aligned (four outputs per store)
   int qc;      // query chunks of at most 8 heads per KV head: ceil(G / 8)
   int head_dim;  // D (the kernel is instantiated per D; kept for host checks)
   unsigned long long wait_ns;  // bound of every mbarrier wait
@@ -289,6 +290,28 @@ __device__ __forceinline__ void store_out(const Params& p, long long idx, float 
     static_cast<__nv_bfloat16*>(p.out)[idx] = __float2bfloat16_rn(v);
   else
     static_cast<__half*>(p.out)[idx] = __float2half_rn(v);
+}
+
+// Four consecutive outputs starting at element idx: one 8-byte store when the
+// output allows it (p.o_al8: base and strides 8-byte aligned, idx a multiple
+// of 4), else four.
+__device__ __forceinline__ void store_out4(const Params& p, long long idx, float a, float b, float c, float d) {
+  if (p.o_al8) {
+    uint2 w;
+    if (p.out_dtype == FK_DTYPE_BF16) {
+      w.x = pack2<true>(a, b);
+      w.y = pack2<true>(c, d);
+    } else {
+      w.x = pack2<false>(a, b);
+      w.y = pack2<false>(c, d);
+    }
+    *reinterpret_cast<uint2*>(static_cast<unsigned short*>(p.out) + idx) = w;
+  } else {
+    store_out(p, idx, a);
+    store_out(p, idx + 1, b);
+    store_out(p, idx + 2, c);
+    store_out(p, idx + 3, d);
+  }
 }
 
 // Normalisation of query head qh with the oracle's sink formula.  L and the
@@ -823,10 +846,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           const long long ob = obase + static_cast<long long>(qh) * p.o_sh + d4;
 #pragma unroll
           for (int k = 0; k < D / 32; ++k) {
-            store_out(p, ob + 32 * k + 0, norm_out(A[k].x, e, Lf, sv));
-            store_out(p, ob + 32 * k + 1, norm_out(A[k].y, e, Lf, sv));
-            store_out(p, ob + 32 * k + 2, norm_out(A[k].z, e, Lf, sv));
-            store_out(p, ob + 32 * k + 3, norm_out(A[k].w, e, Lf, sv));
+            store_out4(p, ob + 32 * k, norm_out(A[k].x, e, Lf, sv), norm_out(A[k].y, e, Lf, sv),
+                       norm_out(A[k].z, e, Lf, sv), norm_out(A[k].w, e, Lf, sv));
           }
         } else {
           float4* dst = reinterpret_cast<float4*>(&ws_acc[(static_cast<long long>(mt.seg) * GMAX + hs) * HEAD_DIM + d4]);
@@ -900,7 +921,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
         float e, Lf;
         sink_norm(L, M, p.s_aux, qh, &e, &Lf);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) store_out(p, ob + i, norm_out(A[i], e, Lf, sv));
+        for (int i = 0; i < 16; i += 4)
+          store_out4(p, ob + i, norm_out(A[i], e, Lf, sv), norm_out(A[i + 1], e, Lf, sv),
+                     norm_out(A[i + 2], e, Lf, sv), norm_out(A[i + 3], e, Lf, sv));
       }
       if (et == 0) cnt[item] = 0;
     }
