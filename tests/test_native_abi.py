@@ -62,3 +62,10 @@ def test_entry_points_reject_cpu_tensors():
     k = torch.zeros(4, 8, 128, dtype=torch.float16)
     with pytest.raises(ValueError, match="CUDA"):
         fk.flash_decode_gqa_varlen(q, k, k, torch.tensor([0, 4], dtype=torch.int32))
+
+
+def test_debug_hook_validates_its_arguments():
+    L = N.lib()
+    assert L.fk_debug_configure(10, 0) == 1 and "wait_ns" in N.last_error()
+    assert L.fk_debug_configure(4_000_000_000, 2) == 1 and "inject" in N.last_error()
+    assert L.fk_debug_configure(4_000_000_000, 0) == 0  # the default: 4 s bound, no injection
