@@ -115,7 +115,7 @@ def setup_workload(name, rank, world, device):
     if name in ("config2", "config2s", "config2g16", "config2d64"):
         # config2g16 / config2d64: config 2's lengths with a 16-head GQA group
         # (128 query heads) / with head dim 64 (64 query heads), shapes the
-        # reference's Triton kernels take beyond BASELINE's configs
+        # reference's Triton kernels take beyond the benchmark configs
         spec = W.CONFIGS[2]
         lens = W.config_lengths(2, seed=0)
         if name == "config2s":  # profiling case: first 8 sequences (~0.4 GB of KV, still > L2)

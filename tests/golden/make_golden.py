@@ -28,7 +28,9 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = os.environ.get("FK_REFERENCE", "/root/reference")
+REF = os.environ.get("FK_REFERENCE")
+if not REF:
+    raise SystemExit("set FK_REFERENCE to a checkout of the reference (coder0143/fasterkernels)")
 sys.path.insert(0, REF)
 OUT_DIR = os.path.dirname(os.path.abspath(__file__))
 
@@ -159,7 +161,7 @@ def fp8_case(name, seed, B, QH, KVH, S, lens, splits):
 
 
 def config1_case():
-    """BASELINE config 1 (fp32, CPU): only the output and input checksums are
+    """Benchmark config 1 (fp32, CPU): only the output and input checksums are
     stored; the inputs are regenerated from the seed protocol (generator seed
     0: lengths, then q, k, v, s_aux)."""
     g = torch.Generator().manual_seed(0)
@@ -190,7 +192,7 @@ CASES = {
     "dense_g4_window": lambda: dense_case("dense_g4_window", 7, 2, 8, 2, 96, [90, 50], [10, 0], 4),
     "fp8_g4": lambda: fp8_case("fp8_g4", 8, 2, 8, 2, 160, [150, 77], 2),
     "config1": config1_case,
-    # shapes beyond BASELINE's: a 16-head group (K1 pads it to BLOCK_H = 16)
+    # shapes beyond the benchmark configs: a 16-head group (K1 pads it to BLOCK_H = 16)
     # and head dim 64 (K1 and K6 take any power of two)
     "varlen_g16_nosink": lambda: varlen_case("varlen_g16_nosink", 9, [70, 1, 150], 32, 2, None, True),
     "varlen_g8_d64_nosink": lambda: varlen_case("varlen_g8_d64_nosink", 10, [90, 3, 200], 16, 2, None, True, hd=64),

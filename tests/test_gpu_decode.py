@@ -308,7 +308,7 @@ def test_hf_adapters_head_dim_64(dev):
         close(out, ref, **BF16_TOL)
 
 
-# ------------------------------------------------- full BASELINE sizes
+# ------------------------------------------------- full benchmark sizes
 def test_config2_full_size(dev):
     lens = W.config_lengths(2)
     assert sum(lens) == 377152

@@ -79,7 +79,7 @@ def test_fp8_oracle_matches_reference():
 
 
 def test_config1_oracle_matches_reference():
-    """BASELINE config 1 regenerated from the seed protocol; output pinned."""
+    """Benchmark config 1 (the CPU-sized case) regenerated from the seed protocol; output pinned."""
     z = load("config1_sink_fp32")
     g = torch.Generator().manual_seed(0)
     lens = torch.randint(1, 2049, (4,), generator=g)
