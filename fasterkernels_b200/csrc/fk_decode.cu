@@ -17,6 +17,15 @@
 
 #include "fk_decode_kernel.cuh"
 
+// The kernels are instantiated in fk_kernels_{f16,bf16,e4m3}.cu; a build of
+// this file alone (e.g. the -DFK_TRACE diagnostics build) defines
+// FK_SINGLE_TU and instantiates them here.
+#ifndef FK_SINGLE_TU
+FK_KERNELS_F16(FK_KERNEL_DECL)
+FK_KERNELS_BF16(FK_KERNEL_DECL)
+FK_KERNELS_E4M3(FK_KERNEL_DECL)
+#endif
+
 namespace fk {
 
 // ------------------------------------------------------------------------

@@ -1211,3 +1211,20 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 }
 
 }  // namespace fk
+
+// Every kernel instantiation the host side launches, per KV element type:
+// X(KV, LAYOUT, HP, D, CP, QC).  Each list is explicitly instantiated in its
+// own translation unit (fk_kernels_<type>.cu) so that the three compile in
+// parallel; fk_decode.cu declares them extern.
+#define FK_KERNELS_LAYOUTS(X, KVT, H, DD, CC, QQ) \
+  X(KVT, 0, H, DD, CC, QQ) X(KVT, 1, H, DD, CC, QQ) X(KVT, 2, H, DD, CC, QQ)
+#define FK_KERNELS_HP(X, KVT, DD, QQ)                                                        \
+  FK_KERNELS_LAYOUTS(X, KVT, 1, DD, false, QQ) FK_KERNELS_LAYOUTS(X, KVT, 2, DD, false, QQ) \
+  FK_KERNELS_LAYOUTS(X, KVT, 2, DD, true, QQ)
+#define FK_KERNELS_F16(X) FK_KERNELS_HP(X, FK_DTYPE_F16, 64, false) FK_KERNELS_HP(X, FK_DTYPE_F16, 128, false)
+#define FK_KERNELS_BF16(X) FK_KERNELS_HP(X, FK_DTYPE_BF16, 64, false) FK_KERNELS_HP(X, FK_DTYPE_BF16, 128, false)
+#define FK_KERNELS_E4M3(X) FK_KERNELS_HP(X, FK_DTYPE_E4M3, 128, false) FK_KERNELS_HP(X, FK_DTYPE_E4M3, 128, true)
+#define FK_KERNEL_DECL(KVT, L, H, DD, CC, QQ) \
+  extern template __global__ void fk::decode_split_kernel<KVT, L, H, DD, CC, QQ>(const __grid_constant__ fk::Params);
+#define FK_KERNEL_INST(KVT, L, H, DD, CC, QQ) \
+  template __global__ void fk::decode_split_kernel<KVT, L, H, DD, CC, QQ>(const __grid_constant__ fk::Params);

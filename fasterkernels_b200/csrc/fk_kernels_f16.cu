@@ -1,0 +1,6 @@
+// fk_kernels_f16.cu -- the decode kernel instantiations for F16 KV
+// (compiled apart from the host side so that the kernel sets build in
+// parallel; see fk_decode_kernel.cuh).
+#include "fk_decode_kernel.cuh"
+
+FK_KERNELS_F16(FK_KERNEL_INST)
