@@ -13,7 +13,6 @@
 #include <cstring>
 #include <mutex>
 #include <string>
-#include <unordered_map>
 
 #include "fk_decode_kernel.cuh"
 
@@ -242,56 +241,16 @@ int common_checks(const void* q, const void* k, const void* v, const void* out, 
 std::atomic<unsigned long long> g_wait_ns{4000000000ull};
 std::atomic<int> g_inject{0};
 
-// Programmatic dependent launch of consecutive decode kernels (default on;
-// FK_DECODE_PDL=0 turns it off).
+// Programmatic dependent launch (default on; FK_DECODE_PDL=0 turns it off):
+// the decode grid may be scheduled while the previous kernel of its stream
+// drains, and executes griddepcontrol.wait before its first global read, so
+// whatever that kernel wrote (KV append, RoPE'd Q, new lengths) is visible.
 inline bool pdl_enabled() {
   static const bool on = [] {
     const char* e = getenv("FK_DECODE_PDL");
     return !(e != nullptr && e[0] == '0');
   }();
   return on;
-}
-
-// A decode kernel launched as a programmatic dependent may start while the
-// previous decode kernel of its stream still runs; only its epilogue warps
-// wait for that grid.  Its producer reads Q, the lengths and the block table
-// at once, so a call whose inputs overlap the previous call's output (out
-// fed back as q) is launched without the attribute.  One record per stream.
-struct ByteRange {
-  uintptr_t lo = 0, hi = 0;
-  bool overlaps(const ByteRange& o) const { return lo < o.hi && o.lo < hi; }
-};
-std::mutex g_last_out_mu;
-std::unordered_map<cudaStream_t, ByteRange> g_last_out;
-
-ByteRange span(const void* base, long long last_elem, size_t es) {
-  ByteRange r;
-  if (base == nullptr) return r;
-  r.lo = reinterpret_cast<uintptr_t>(base);
-  r.hi = r.lo + static_cast<uintptr_t>(last_elem + 1) * es;
-  return r;
-}
-
-bool pdl_safe(const Params& p, cudaStream_t stream) {
-  const size_t q_es = (p.q_dtype == FK_DTYPE_E4M3) ? 1 : 2;
-  const long long qh = static_cast<long long>(p.q_heads) - 1, b = static_cast<long long>(p.B) - 1;
-  const ByteRange in[7] = {
-      span(p.q, b * p.q_sb + qh * p.q_sh + p.head_dim - 1, q_es),
-      span(p.lens, p.B, 4),
-      span(p.starts, b, 4),
-      span(p.bt, b * p.bt_sb + p.max_blocks - 1, 4),
-      span(p.scale_q, 0, 4),
-      span(p.scale_k, 0, 4),
-      span(p.s_aux, qh, 4)};
-  const ByteRange out = span(p.out, b * p.o_sb + qh * p.o_sh + p.head_dim - 1, 2);
-  std::lock_guard<std::mutex> lk(g_last_out_mu);
-  auto it = g_last_out.find(stream);
-  bool safe = true;
-  if (it != g_last_out.end())
-    for (const ByteRange& r : in)
-      if (r.hi > r.lo && r.overlaps(it->second)) safe = false;
-  g_last_out[stream] = out;
-  return safe;
 }
 
 template <int KV, int LAYOUT, int HP, int D, bool CP, bool QC>
@@ -305,7 +264,7 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = (pdl_enabled() && pdl_safe(p, stream)) ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_split_kernel<KV, LAYOUT, HP, D, CP, QC>, p);
@@ -420,16 +379,18 @@ extern "C" size_t fk_decode_workspace_bytes(int device, int batch, int kv_heads,
   return fk_decode_workspace_bytes_gqa(device, batch, kv_heads, kv_heads, kv_dtype);
 }
 
-extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, const void* v_varlen,
-                                          const int32_t* cu_seqlens_k, const float* s_aux, void* out, int batch,
-                                          int q_heads, int kv_heads, int head_dim, int64_t total_tokens, int dtype,
-                                          int64_t sq_b, int64_t sq_h, int64_t sk_t, int64_t sk_h, int64_t sv_t,
-                                          int64_t sv_h, int64_t so_b, int64_t so_h, void* workspace,
-                                          size_t workspace_bytes, void* stream) {
-  int device = 0;
+namespace fk {
+
+// Argument checks and tensor maps of a varlen call, everything short of the
+// launch (shared by the workspace and the allocation-free entry points, so
+// that the latter touches its scratch only for a call that will launch).
+// Returns FK_EMPTY for an empty batch.
+int varlen_prepare(Params& p, int* device, const void* q, const void* k_varlen, const void* v_varlen,
+                   const int32_t* cu_seqlens_k, const float* s_aux, void* out, int batch, int q_heads, int kv_heads,
+                   int head_dim, int64_t total_tokens, int dtype, int64_t sq_b, int64_t sq_h, int64_t sk_t,
+                   int64_t sk_h, int64_t sv_t, int64_t sv_h, int64_t so_b, int64_t so_h, void* workspace) {
   int rc = common_checks(q, k_varlen, v_varlen, out, batch, q_heads, kv_heads, head_dim, dtype, dtype, dtype,
-                         workspace, &device);
-  if (rc == FK_EMPTY) return FK_OK;
+                         workspace, device);
   if (rc != FK_OK) return rc;
   if ((rc = check_q_align(q, dtype, sq_b, sq_h)) != FK_OK) return rc;
   if (!is16(dtype)) return fail(FK_ERR_UNSUPPORTED, "varlen decode takes f16 or bf16 tensors");
@@ -437,7 +398,6 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
   if (total_tokens < 0 || total_tokens > 0x7fffffffLL) return fail(FK_ERR_INVALID_ARG, "bad total_tokens");
   if (((sk_t | sk_h | sv_t | sv_h) * 2) % 16 != 0)
     return fail(FK_ERR_INVALID_ARG, "k/v strides must be multiples of 16 bytes");
-  Params p;
   memset(&p, 0, sizeof(p));
   fill_common(p, q, sq_b, sq_h, out, so_b, so_h, s_aux, batch, q_heads, kv_heads, head_dim, dtype, dtype, nullptr, nullptr,
               nullptr, workspace);
@@ -453,7 +413,24 @@ extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, c
   const uint64_t ks[3] = {static_cast<uint64_t>(sk_t) * 2, 128, static_cast<uint64_t>(sk_h) * 2};
   const uint64_t vs[3] = {static_cast<uint64_t>(sv_t) * 2, 128, static_cast<uint64_t>(sv_h) * 2};
   if ((rc = encode_map(&p.tk, dtype, 4, k_varlen, dims, ks, box)) != FK_OK) return rc;
-  if ((rc = encode_map(&p.tv, dtype, 4, v_varlen, dims, vs, box)) != FK_OK) return rc;
+  return encode_map(&p.tv, dtype, 4, v_varlen, dims, vs, box);
+}
+
+}  // namespace fk
+
+extern "C" int fk_flash_decode_gqa_varlen(const void* q, const void* k_varlen, const void* v_varlen,
+                                          const int32_t* cu_seqlens_k, const float* s_aux, void* out, int batch,
+                                          int q_heads, int kv_heads, int head_dim, int64_t total_tokens, int dtype,
+                                          int64_t sq_b, int64_t sq_h, int64_t sk_t, int64_t sk_h, int64_t sv_t,
+                                          int64_t sv_h, int64_t so_b, int64_t so_h, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  int device = 0;
+  Params p;
+  const int rc = varlen_prepare(p, &device, q, k_varlen, v_varlen, cu_seqlens_k, s_aux, out, batch, q_heads, kv_heads,
+                                head_dim, total_tokens, dtype, sq_b, sq_h, sk_t, sk_h, sv_t, sv_h, so_b, so_h,
+                                workspace);
+  if (rc == FK_EMPTY) return FK_OK;
+  if (rc != FK_OK) return rc;
   return launch<VARLEN>(p, dtype, device, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -671,43 +648,59 @@ extern "C" int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_v
                                                   int64_t total_tokens, int dtype, int64_t sq_b, int64_t sq_h,
                                                   int64_t sk_t, int64_t sk_h, int64_t sv_t, int64_t sv_h,
                                                   int64_t so_b, int64_t so_h, void* stream) {
-  if (batch == 0) return FK_OK;
-  if (k_varlen == nullptr) return fail(FK_ERR_INVALID_ARG, "q, k, v and out must be non-null");
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, k_varlen) != cudaSuccess || attr.type != cudaMemoryTypeDevice) {
-    cudaGetLastError();
-    return fail(FK_ERR_INVALID_ARG, "k must be device memory");
-  }
-  const int device = attr.device;
-  if (batch < 0 || kv_heads <= 0) return fail(FK_ERR_INVALID_ARG, "bad sizes: batch=%d kv_heads=%d", batch, kv_heads);
-  if (q_heads <= 0 || q_heads % kv_heads != 0)
-    return fail(FK_ERR_INVALID_ARG, "q_heads (%d) must be a positive multiple of kv_heads (%d)", q_heads, kv_heads);
+  // Every argument is checked (and the tensor maps built) before the scratch
+  // is touched: a refused call queues nothing on the stream.  The workspace
+  // argument of the checks only has to be non-null here.
+  int device = 0;
+  Params p;
+  int rc = varlen_prepare(p, &device, q, k_varlen, v_varlen, cu_seqlens_k, s_aux, out, batch, q_heads, kv_heads,
+                          head_dim, total_tokens, dtype, sq_b, sq_h, sk_t, sk_h, sv_t, sv_h, so_b, so_h,
+                          reinterpret_cast<void*>(uintptr_t(1)));
+  if (rc == FK_EMPTY) return FK_OK;
+  if (rc != FK_OK) return rc;
   const int qc = qc_for(q_heads, kv_heads);
   const int hp = hp_for(kv_heads, qc);
-  const int S = num_work_ctas_any_d(device, dtype == FK_DTYPE_BF16 ? FK_DTYPE_BF16 : FK_DTYPE_F16, hp, hp == 2 && qc > 1);
+  const int S = num_work_ctas(device, dtype, hp, head_dim, hp == 2 && qc > 1);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
-  const size_t need = WsLayout::min_bytes(batch, kv_heads * qc, S);
-  if (need > NOALLOC_SCRATCH_BYTES)
+  const long long items = static_cast<long long>(batch) * kv_heads * qc;
+  const WsLayout wl(NOALLOC_SCRATCH_BYTES, batch, kv_heads * qc, S);
+  if (!wl.fits(NOALLOC_SCRATCH_BYTES, batch, kv_heads * qc))
     return fail(FK_ERR_WORKSPACE,
-                "batch*kv_heads = %lld needs %zu bytes of scratch; the allocation-free entry point has a fixed "
-                "%zu-byte scratch (batch*kv_heads + %d <= %zu)",
-                static_cast<long long>(batch) * kv_heads, need, NOALLOC_SCRATCH_BYTES, S,
+                "batch*kv_heads*ceil(G/8) = %lld needs %zu bytes of scratch; the allocation-free entry point has a "
+                "fixed %zu-byte scratch, which holds batch*kv_heads*ceil(G/8) + %d (resident CTAs) <= %zu",
+                items, WsLayout::min_bytes(batch, kv_heads * qc, S), NOALLOC_SCRATCH_BYTES, S,
                 (NOALLOC_SCRATCH_BYTES - 256 - 1024) / SEG_BYTES);
   void* scratch = nullptr;
-  int rc = noalloc_scratch(device, &scratch);
-  if (rc != FK_OK) return rc;
-  // The status word and the arrival counters must start at zero: clear them on
-  // the caller's stream (a memset, not an allocation).
-  const WsLayout wl(NOALLOC_SCRATCH_BYTES, batch, kv_heads * qc, S);
+  if ((rc = noalloc_scratch(device, &scratch)) != FK_OK) return rc;
+  p.ws = static_cast<unsigned char*>(scratch);
+  // The arrival counters must start at zero: clear them on the caller's
+  // stream (a memset, not an allocation).  The status word before them is
+  // left alone: it collects FK_STATUS_* bits until fk_noalloc_read_status
+  // clears it.
   int prev = 0;
   cudaGetDevice(&prev);
   if (prev != device) cudaSetDevice(device);
-  const cudaError_t e = cudaMemsetAsync(scratch, 0, wl.ml, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaMemsetAsync(static_cast<unsigned char*>(scratch) + wl.cnt, 0, wl.ml - wl.cnt,
+                                        static_cast<cudaStream_t>(stream));
   if (prev != device) cudaSetDevice(prev);
   if (e != cudaSuccess) return fail(FK_ERR_CUDA, "clearing the scratch failed: %s", cudaGetErrorString(e));
-  return fk_flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux, out, batch, q_heads, kv_heads,
-                                    head_dim, total_tokens, dtype, sq_b, sq_h, sk_t, sk_h, sv_t, sv_h, so_b, so_h,
-                                    scratch, NOALLOC_SCRATCH_BYTES, stream);
+  return launch<VARLEN>(p, dtype, device, NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fk_noalloc_read_status(int device, int* status, int clear) {
+  if (status == nullptr) return fail(FK_ERR_INVALID_ARG, "status must be non-null");
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(device, &scratch);
+  if (rc != FK_OK) return rc;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(status, scratch, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear && *status != 0) e = cudaMemset(scratch, 0, sizeof(int));
+  if (prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(FK_ERR_CUDA, "reading the scratch status failed: %s", cudaGetErrorString(e));
+  return FK_OK;
 }
 
 #ifdef FK_TRACE

@@ -425,6 +425,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       reinterpret_cast<uint4*>(qstage + sh * (GPAD * 64) + j * 64)[c] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+  // Programmatic dependent launch: this grid may start while the kernel
+  // before it in the stream (a decode call, a KV append, a RoPE or projection
+  // kernel) is still running.  Nothing above reads global memory; every input
+  // (lengths, block table, Q, K/V, sinks, scales) is read after this wait,
+  // which returns once the prerequisite grid has completed and its writes are
+  // visible.
+  grid_dependency_wait();
   // Plan, with every thread of the CTA: thread t sums the granules of
   // sequences [t*bpt, (t+1)*bpt) (independent loads, one round trip); warp 0
   // turns the per-thread sums into exclusive prefixes.
@@ -454,8 +461,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 #ifdef FK_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][16] = gtimer();
 #endif
-  // Let the next decode kernel in the stream start its CTAs (planning and
-  // KV loads) as SMs free up; its epilogue warps wait for this grid.
+  // Let the next kernel in the stream start its CTAs as SMs free up (it
+  // waits for this grid's completion before reading anything).
   grid_dependency_trigger();
 
   if (warp == CWARPS) {
@@ -479,9 +486,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
     bool alive = true;
     // Test hook (off unless the host sets it): publish nothing for the first
     // stage, so the consumers' bounded wait on it runs out and the kernel
-    // returns with FK_STATUS_TIMEOUT.  Nothing is left in flight: no copy
-    // is issued for that stage.
+    // returns with FK_STATUS_TIMEOUT.  The later stages' copies are still
+    // issued; on any timeout exit the producer waits (bounded) for every
+    // stage it armed to land before the CTA leaves (see the end of this
+    // branch).
     bool withhold = p.inject == 1;
+    // Stages armed with copies (bit s) and the phase parity each was armed in.
+    uint32_t armed = 0, armed_par = 0;
     // Claim the next ring slot (waits for the consumers to release it).
     auto acquire = [&]() -> bool {
       int ok = 1;
@@ -679,6 +690,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
             mt.nseg = nseg;
             mbar_arrive_expect_tx(fb, bytes);
           }
+          armed |= 1u << stage;
+          armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
           __syncwarp();
           if constexpr (LAYOUT == PAGED) {
             if (phys >= 0) {
@@ -753,6 +766,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
         meta[stage].flags = F_END;
         mbar_arrive(smem_u32(&full[stage]));
       }
+    } else if (lane == 0) {
+      // A wait ran out: copies the consumers will never wait for may still be
+      // in flight into this CTA's shared memory.  Let them land (each wait
+      // bounded) before the CTA exits.
+      for (int s2 = 0; s2 < C::STAGES; ++s2)
+        if ((armed >> s2) & 1u) mbar_wait(smem_u32(&full[s2]), (armed_par >> s2) & 1u, p.wait_ns);
     }
     return;
   }
@@ -765,9 +784,6 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
     // segments (CTA order: the result is deterministic) and re-arm its
     // arrival counter.
     const int et = threadIdx.x - (CWARPS + 1) * 32;  // 0 .. ETHREADS-1
-    // Only these warps write global memory: wait until the previous kernel
-    // in the stream (if launched as its programmatic dependent) has finished.
-    grid_dependency_wait();
     // Sequences of length 0 own no granules: CTA b % S writes their zero rows.
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       long long t0;

@@ -166,9 +166,27 @@ def _fallback(module, query_states, key_states, value_states, attention_mask, sc
                                        dropout, **kwargs)
 
 
+def _check_scaling(scaling, head_dim):
+    """The kernels scale logits by head_dim ** -0.5, as the reference's HF
+    adapters do whatever ``scaling`` says (triton_gqa_decode_hf.py:50).  A
+    model whose attention uses another scale would get wrong attention, so
+    such a call is refused instead of silently decoded."""
+    if scaling is None:
+        return
+    want = float(head_dim) ** -0.5
+    if abs(float(scaling) - want) > 1e-4 * want:
+        raise ValueError(f"attention scaling {float(scaling)!r} is not head_dim**-0.5 = {want!r}; the decode "
+                         "kernels only implement the 1/sqrt(head_dim) softmax scale")
+
+
 def _is_decode(kwargs, query_states):
-    return (query_states.shape[2] == 1 and query_states.is_cuda and query_states.shape[-1] in HEAD_DIMS
-            and (kwargs.get("past_key_values") is not None or kwargs.get("cache_position") is not None))
+    """One query token per sequence on the GPU: attention over every cached
+    key (bounded by the window that _decode_window derives) is exactly what
+    the decode kernel computes.  The reference also requires a
+    ``past_key_values`` keyword (triton_gqa_decode_hf.py:236), which
+    transformers 5.x no longer passes to attention functions, so its adapter
+    never engages under ``generate``; this one does."""
+    return query_states.shape[2] == 1 and query_states.is_cuda and query_states.shape[-1] in HEAD_DIMS
 
 
 def custom_hf_decode_attention_forward(module, query_states, key_states, value_states, attention_mask, scaling: float,
@@ -179,6 +197,7 @@ def custom_hf_decode_attention_forward(module, query_states, key_states, value_s
     (triton_gqa_decode_hf.py:218-258); anything else goes to transformers' SDPA."""
     bsz, q_heads, q_len, head_dim = query_states.shape
     if _is_decode(kwargs, query_states):
+        _check_scaling(scaling, head_dim)
         q = query_states.squeeze(2)
         lens, starts = _decode_window(kwargs, bsz, q.device, attention_mask, key_states.shape[2])
         out = dense_decode(q, key_states, value_states, lens, starts,
@@ -187,14 +206,17 @@ def custom_hf_decode_attention_forward(module, query_states, key_states, value_s
     return _fallback(module, query_states, key_states, value_states, attention_mask, scaling, dropout, **kwargs)
 
 
-def register_attention_interface(name: str = "fk_decode", fp8: bool = False) -> str:
+def register_attention_interface(name: str = "fk_decode", fp8: bool = False, paged: bool = False) -> str:
     """Register the adapter with transformers' ``AttentionInterface`` so that
     ``attn_implementation=name`` selects it for any model (the reference's
     module-global patch of ``eager_attention_forward``,
     fskernels/engine/fs_inference_engine.py:12-13, only takes effect under
-    "eager" in transformers 5.x).  Returns the registered name."""
+    "eager" in transformers 5.x).  ``paged=True`` registers the paged-cache
+    adapter (``custom_paged_attention_forward``).  Returns the registered name."""
     from transformers import AttentionInterface
-    if fp8:
+    if paged:
+        from .paged_attn.paged_adapter import custom_paged_attention_forward as fn
+    elif fp8:
         from .gqa_decode_hf_fp8 import custom_hf_decode_attention_forward_fp8 as fn
     else:
         fn = custom_hf_decode_attention_forward

@@ -20,8 +20,8 @@ from typing import Optional, Tuple
 import torch
 
 from .gqa_decode import HEAD_DIM
-from .gqa_decode_hf import (_decode_window, _fallback, _is_decode, _module_sinks, custom_hf_decode_attention_forward,
-                            dense_decode)
+from .gqa_decode_hf import (_check_scaling, _decode_window, _fallback, _is_decode, _module_sinks,
+                            custom_hf_decode_attention_forward, dense_decode)
 
 FP8_DTYPE = torch.float8_e4m3fn
 FP8_MAX = 448.0
@@ -74,6 +74,7 @@ def custom_hf_decode_attention_forward_fp8(module, query_states, key_states, val
         return custom_hf_decode_attention_forward(module, query_states, key_states, value_states, attention_mask,
                                                   scaling, dropout, **kwargs)
     if _is_decode(kwargs, query_states):
+        _check_scaling(scaling, head_dim)
         out_dtype = query_states.dtype
         q = query_states.squeeze(2)
         lens, starts = _decode_window(kwargs, bsz, q.device, attention_mask, key_states.shape[2])

@@ -100,6 +100,37 @@ class PagedKVCache:
         self.v_pool[layer_idx, pp, :, off, :] = v[0, :, 0, :]
         self._seq_lens[seq_id] = pos + 1
 
+    def write_prefill(self, seq_id: int, layer_idx: int, k: torch.Tensor, v: torch.Tensor, reserve: int = 0) -> None:
+        """Write a prompt's K/V ([KV_H, T, D]) as tokens 0..T-1 of one layer of
+        a sequence, with one indexed copy per pool (the reference appends the
+        prompt token by token, benchmarks/run_hf_triton_fp8_paged.py:113-117).
+        Pages are allocated on the host for max(T, reserve) tokens, so a
+        caller can fix the block table for the decode steps that follow.
+        The sequence length becomes T (the same T for every layer)."""
+        if k.dim() != 3 or k.shape != v.shape or k.shape[0] != self.num_kv_heads or k.shape[2] != self.head_dim:
+            raise ValueError("k / v must be [num_kv_heads, T, head_dim]")
+        T = int(k.shape[1])
+        pages = self._pages[seq_id]
+        need = (max(T, int(reserve)) + PAGE_SIZE - 1) // PAGE_SIZE
+        if need > self.max_blocks_per_seq:
+            raise RuntimeError("sequence exceeds max_blocks_per_seq")
+        if need > len(pages):
+            new = [self._alloc_page() for _ in range(need - len(pages))]
+            first = len(pages)
+            pages.extend(new)
+            self.block_table[seq_id, first:need] = torch.tensor(new, dtype=torch.int32).to(self.device)
+        if T > 0:
+            tok = torch.arange(T)
+            phys = torch.tensor(pages, dtype=torch.long)[tok // PAGE_SIZE].to(self.device)
+            slot = (tok % PAGE_SIZE).to(self.device)
+            kt, vt = k.transpose(0, 1), v.transpose(0, 1)  # [T, KV_H, D]
+            if self.dtype == torch.float8_e4m3fn:
+                kt = (kt.float() / self.k_scale).clamp(-448.0, 448.0).to(self.dtype)
+                vt = (vt.float() / self.v_scale).clamp(-448.0, 448.0).to(self.dtype)
+            self.k_pool[layer_idx][phys, :, slot, :] = kt.to(self.dtype)
+            self.v_pool[layer_idx][phys, :, slot, :] = vt.to(self.dtype)
+        self._seq_lens[seq_id] = T
+
     def set_fp8_scales(self, k_scale, v_scale) -> None:
         """Per-tensor scales of an e4m3 pool (value = e4m3 x scale), e.g. amax / 448
         of calibration K/V."""

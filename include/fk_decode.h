@@ -202,12 +202,15 @@ int fk_profile_end(float* kernel_ms, int* launches);
  * host framework owns every allocation, or a process where cudaMalloc is not
  * allowed once serving starts -- the scratch comes from a fixed array inside
  * the library (fk_noalloc_scratch_bytes() bytes, 8 MiB, held on every GPU that
- * loads the library until exit).  It fits batch * kv_heads + (resident CTAs)
- * <= about 1000 segments (about 850 sequence-head pairs for 16-bit KV);
- * larger calls return FK_ERR_WORKSPACE.
+ * loads the library until exit).  It holds
+ *   batch * kv_heads * ceil(G / 8) + (resident CTAs, 148 on a B200)
+ *     <= (fk_noalloc_scratch_bytes() - 1280) / 8324  (= 1007 segments),
+ * G = q_heads / kv_heads: about 850 sequence-head pairs for G <= 8, half that
+ * for 8 < G <= 16.  Larger calls return FK_ERR_WORKSPACE and queue nothing.
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture.  Each call clears the scratch's
- * status word and counters on `stream`.  All calls share the one array, so
+ * arrival counters on `stream`; the status word collects FK_STATUS_* bits
+ * until fk_noalloc_read_status clears it.  All calls share the one array, so
  * calls that overlap on the GPU (different streams, or different threads)
  * race: serialise them.  Nothing is allocated: no cudaMalloc/cudaFree.
  */
@@ -223,6 +226,15 @@ int fk_flash_decode_gqa_varlen_noalloc(const void* q, const void* k_varlen, cons
 /* Bytes of the fixed scratch used by fk_flash_decode_gqa_varlen_noalloc. */
 size_t fk_noalloc_scratch_bytes(void);
 
+/*
+ * Status of the allocation-free entry point on `device` (no counterpart in
+ * the reference): the OR of FK_STATUS_* bits (FK_STATUS_TIMEOUT when a
+ * bounded wait ran out and the output is incomplete) set by its calls since
+ * the last clear.  Waits for the device to finish its work (keep it off the
+ * hot path); clear != 0 then zeroes the word.
+ */
+int fk_noalloc_read_status(int device, int* status, int clear);
+
 /* Size of the persistent decode grid (resident CTAs) on `device` for this
  * KV element type and KV head count. */
 int fk_decode_num_ctas(int device, int kv_dtype, int kv_heads);
@@ -232,8 +244,8 @@ int fk_decode_num_ctas(int device, int kv_dtype, int kv_heads);
  * reference).  wait_ns bounds every mbarrier wait of later launches (default
  * 4 s, range [1 ms, 60 s]); inject = 1 makes each CTA's producer publish
  * nothing for its first pipeline stage, so its consumers' wait runs out, the
- * kernel sets FK_STATUS_TIMEOUT and returns (no fault, nothing left in
- * flight).  Clear the workspace after a timeout: arrival counters of split
+ * kernel sets FK_STATUS_TIMEOUT and returns (no fault; before exiting, each
+ * CTA waits, bounded, for the copies it issued to land).  Clear the workspace after a timeout: arrival counters of split
  * items may be left mid-count.  inject = 0 restores normal operation.
  */
 int fk_debug_configure(unsigned long long wait_ns, int inject);

@@ -315,7 +315,11 @@ def test_config2_full_size(dev):
     d = W.make_varlen(lens, 32, 8, torch.float16, dev, seed=0, sinks=True)
     out = fk.flash_decode_gqa_varlen(d["q"], d["k"], d["v"], d["cu_seqlens"], d["s_aux"])
     cu = d["cu_seqlens"].cpu().numpy()
-    for b in (0, 17, 31):  # spot-check whole sequences against the oracle
+    # spot-check whole sequences against the oracle: the longest, the
+    # shortest and six more spread over the batch
+    picks = sorted({int(np.argmax(lens)), int(np.argmin(lens)), 0, 5, 11, 17, 24, 31})
+    assert len(picks) >= 8
+    for b in picks:
         lo, hi = cu[b], cu[b + 1]
         ref = O.decode_varlen(d["q"][b:b + 1].float().cpu().numpy(), d["k"][lo:hi].float().cpu().numpy(),
                               d["v"][lo:hi].float().cpu().numpy(), np.array([0, hi - lo]), d["s_aux"].cpu().numpy())
@@ -335,7 +339,9 @@ def test_config3_full_size_paged_equals_varlen(dev):
     outv = fk.flash_decode_gqa_varlen(d["q"], d["k"], d["v"], d["cu_seqlens"])
     assert torch.equal(outp, outv)
     cu = d["cu_seqlens"].cpu().numpy()
-    for b in (0, 63):
+    picks = sorted({int(np.argmax(lens)), int(np.argmin(lens)), 0, 9, 21, 33, 47, 63})
+    assert len(picks) >= 8
+    for b in picks:
         lo, hi = cu[b], cu[b + 1]
         ref = O.decode_varlen(d["q"][b:b + 1].float().cpu().numpy(), d["k"][lo:hi].float().cpu().numpy(),
                               d["v"][lo:hi].float().cpu().numpy(), np.array([0, hi - lo]))
@@ -362,6 +368,50 @@ def test_config4_full_size_fp8_paged_equals_dense(dev):
                               d["s_aux"].cpu().numpy())
         close(outp[b:b + 1], ref, **FP8_TOL)
     assert N.read_status(dev) == 0
+
+
+def test_config5_full_size_fp8_paged_sinks(dev):
+    # the multi-GPU benchmark configuration at its own size on one GPU:
+    # B=128, Q_H=64, KV_H=8 (G=8), lengths log-U[4096, 131072], e4m3 paged
+    # with sinks, pool x1.25 in a random page order
+    spec = W.CONFIGS[5]
+    lens = W.config_lengths(5)
+    assert len(lens) == 128 and max(lens) <= 131072 and min(lens) >= 4096
+    d = W.make_varlen(lens, spec.q_heads, spec.kv_heads, torch.float16, dev, seed=0, sinks=True)
+    q, s_aux, cu_t = d["q"], d["s_aux"], d["cu_seqlens"]
+    k8, sk = W.quantize_e4m3(d["k"])
+    del d["k"]
+    v8, sv = W.quantize_e4m3(d["v"])
+    del d["v"]
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=0)
+    kp, vp = kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn)
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    outp = fk.paged_flash_decode(q, kp, vp, bt, sl, 16, s_aux=s_aux, scale_k=sk, scale_v=sv)
+    torch.cuda.synchronize()
+    assert N.read_status(dev) == 0
+    del kp, vp
+    # the same logical KV on the HF dense cache: bit-identical
+    cu = cu_t.cpu().numpy()
+    S = max(lens)
+    kc = torch.zeros(len(lens), spec.kv_heads, S, 128, dtype=torch.uint8, device=dev)
+    vc = torch.zeros_like(kc)
+    for b, L in enumerate(lens):
+        kc[b, :, :L] = k8[cu[b]:cu[b + 1]].view(torch.uint8).transpose(0, 1)
+        vc[b, :, :L] = v8[cu[b]:cu[b + 1]].view(torch.uint8).transpose(0, 1)
+    outd = fk.flash_decode_gqa_hf_fp8(q, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), sl, None, sk, sv,
+                                      torch.float16, s_aux=s_aux)
+    torch.cuda.synchronize()
+    assert torch.equal(outp, outd)
+    assert N.read_status(dev) == 0
+    del kc, vc
+    # the oracle on the dequantised KV: longest, shortest and two median sequences
+    order = np.argsort(lens)
+    picks = [int(order[-1]), int(order[0]), int(order[len(lens) // 2 - 1]), int(order[len(lens) // 2])]
+    for b in picks:
+        lo, hi = cu[b], cu[b + 1]
+        ref = O.decode_varlen(q[b:b + 1].float().cpu().numpy(), (k8[lo:hi].float() * sk).cpu().numpy(),
+                              (v8[lo:hi].float() * sv).cpu().numpy(), np.array([0, hi - lo]), s_aux.cpu().numpy())
+        close(outp[b:b + 1], ref, **FP8_TOL)
 
 
 @pytest.mark.parametrize("kvh", [1, 3])
