@@ -31,8 +31,13 @@ def dev():
 
 
 class _Module:
-    def __init__(self, layer_idx=0, k_scale=None, v_scale=None, sinks=None):
+    """Stands in for an HF attention module (the adapters and the SDPA
+    fallback read only these attributes)."""
+    is_causal = True
+
+    def __init__(self, layer_idx=0, k_scale=None, v_scale=None, sinks=None, groups=4):
         self.layer_idx = layer_idx
+        self.num_key_value_groups = groups
         if k_scale is not None:
             self.k_scale, self.v_scale = k_scale, v_scale
         if sinks is not None:
