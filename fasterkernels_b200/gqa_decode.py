@@ -17,7 +17,8 @@ from __future__ import annotations
 
 import torch
 
-from . import _native as N
+from . import _native as N  # noqa: F401  (loads the library on first use)
+from . import _ops
 
 HEAD_DIM = 128
 HEAD_DIMS = (64, 128)  # 64 with float16/bfloat16 KV only
@@ -83,13 +84,5 @@ def flash_decode_gqa_varlen(q, k_varlen, v_varlen, cu_seqlens_k, s_aux=None, *, 
         out = torch.empty(B, QH, D, dtype=q.dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != q.dtype or out.stride(-1) != 1:
         raise ValueError("out must be [B, Q_H, D] of q's dtype with unit inner stride")
-    code = N.dtype_code(q.dtype)
-    ws = N.workspace(dev, B, QH, KVH, code)
-    rc = N.lib().fk_flash_decode_gqa_varlen(
-        N.ptr(q), N.ptr(k_varlen), N.ptr(v_varlen), N.ptr(cu), N.ptr(s_aux), N.ptr(out),
-        B, QH, KVH, D, T, code,
-        q.stride(0), q.stride(1), k_varlen.stride(0), k_varlen.stride(1),
-        v_varlen.stride(0), v_varlen.stride(1), out.stride(0), out.stride(1),
-        N.ptr(ws), ws.numel(), N.stream_of(dev))
-    N.check(rc, "fk_flash_decode_gqa_varlen")
+    _ops.varlen(q, k_varlen, v_varlen, cu, s_aux, out)
     return out

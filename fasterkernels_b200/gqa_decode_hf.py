@@ -21,6 +21,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _native as N
+from . import _ops
 from .gqa_decode import HEAD_DIMS, _check_idx, _check_sink, _inner_contig
 
 _DECODE_NUM_SPLITS: int = 1
@@ -89,14 +90,7 @@ def dense_decode(q, k_cache, v_cache, cache_lens, start_k_offsets=None, *, s_aux
         out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
         raise ValueError("out must be [B, Q_H, D] of out_dtype with unit inner stride")
-    ws = N.workspace(dev, B, QH, KVH, kv_code)
-    rc = N.lib().fk_flash_decode_gqa_hf_dense(
-        N.ptr(q), N.ptr(k_cache), N.ptr(v_cache), N.ptr(lens), N.ptr(starts), N.ptr(s_aux), N.ptr(out),
-        B, QH, KVH, D, S, q_code, kv_code, out_code, N.ptr(sq), N.ptr(sk), N.ptr(sv),
-        q.stride(0), q.stride(1), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
-        v_cache.stride(0), v_cache.stride(1), v_cache.stride(2), out.stride(0), out.stride(1),
-        N.ptr(ws), ws.numel(), N.stream_of(dev))
-    N.check(rc, "fk_flash_decode_gqa_hf_dense")
+    _ops.dense(q, k_cache, v_cache, lens, starts, s_aux, sq, sk, sv, out)
     return out
 
 

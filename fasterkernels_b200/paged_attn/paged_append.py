@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native as N
+from .. import _ops
 
 
 def paged_kv_append(k_new, v_new, k_pool, v_pool, block_table, positions, *, scale_k=None, scale_v=None,
@@ -48,10 +49,4 @@ def paged_kv_append(k_new, v_new, k_pool, v_pool, block_table, positions, *, sca
             raise ValueError("an e4m3 pool needs scale_k and scale_v")
         sk = scale_k.reshape(()).to(torch.float32).contiguous()
         sv = scale_v.reshape(()).to(torch.float32).contiguous()
-    rc = N.lib().fk_paged_kv_append(
-        N.ptr(k_new), N.ptr(v_new), N.dtype_code(k_new.dtype), N.ptr(k_pool), N.ptr(v_pool), pool_code, N.ptr(bt),
-        N.ptr(positions), 1 if increment else 0, N.ptr(sk), N.ptr(sv), N.ptr(status), B, KVH, D, k_pool.shape[0],
-        bt.shape[1], k_new.stride(0), k_new.stride(1), v_new.stride(0), v_new.stride(1), k_pool.stride(0),
-        k_pool.stride(1), k_pool.stride(2), v_pool.stride(0), v_pool.stride(1), v_pool.stride(2), bt.stride(0),
-        N.stream_of(k_new.device))
-    N.check(rc, "fk_paged_kv_append")
+    _ops.append(k_new, v_new, k_pool, v_pool, bt, positions, bool(increment), sk, sv, status)

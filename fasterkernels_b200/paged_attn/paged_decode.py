@@ -14,6 +14,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native as N
+from .. import _ops
 from ..gqa_decode import HEAD_DIMS, _check_idx, _check_sink, _inner_contig
 from ..gqa_decode_hf import _scale_ptr
 
@@ -63,12 +64,5 @@ def paged_flash_decode(q, k_pool, v_pool, block_table, seq_lens, page_size, *, s
         out = torch.empty(B, QH, D, dtype=out_dtype, device=dev)
     elif out.shape != (B, QH, D) or out.dtype != out_dtype or out.stride(-1) != 1:
         raise ValueError("out must be [B, Q_H, D] of out_dtype with unit inner stride")
-    ws = N.workspace(dev, B, QH, KVH, kv_code)
-    rc = N.lib().fk_paged_flash_decode(
-        N.ptr(q), N.ptr(k_pool), N.ptr(v_pool), N.ptr(bt), N.ptr(lens), N.ptr(s_aux), N.ptr(out),
-        B, QH, KVH, D, P, PS, bt.shape[1], q_code, kv_code, out_code, N.ptr(sq), N.ptr(sk), N.ptr(sv),
-        q.stride(0), q.stride(1), k_pool.stride(0), k_pool.stride(1), k_pool.stride(2),
-        v_pool.stride(0), v_pool.stride(1), v_pool.stride(2), bt.stride(0), out.stride(0), out.stride(1),
-        N.ptr(ws), ws.numel(), N.stream_of(dev))
-    N.check(rc, "fk_paged_flash_decode")
+    _ops.paged(q, k_pool, v_pool, bt, lens, s_aux, sq, sk, sv, out)
     return out
