@@ -622,7 +622,9 @@ def run_sweep(args):
     dev = torch.device("cuda", 0)
     path = os.path.join(ROOT, "baseline", "_ref")
     k1, k1_why = None, None
-    if os.path.isdir(os.path.join(path, "fskernels")):
+    if args.sweep_no_ref:
+        k1_why = "not requested (--sweep-no-ref)"
+    elif os.path.isdir(os.path.join(path, "fskernels")):
         sys.path.insert(0, path)
         try:
             from fskernels.triton.triton_gqa_decode import flash_decode_gqa_varlen as k1
@@ -682,6 +684,7 @@ def main():
     ap.add_argument("--ref-seqs", type=int, default=0, help="reference arm: sequences per step (0 = all)")
     ap.add_argument("--ref-min-seconds", type=float, default=0.0, help="reference arm: keep timing until this long")
     ap.add_argument("--ref-config1", action="store_true", help="reference arm: also time config 1 in full")
+    ap.add_argument("--sweep-no-ref", action="store_true", help="sweep: skip the reference's Triton kernel")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -433,10 +433,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
   // visible.
   grid_dependency_wait();
   // Plan, with every thread of the CTA: thread t sums the granules of
-  // sequences [t*bpt, (t+1)*bpt) (independent loads, one round trip); warp 0
-  // turns the per-thread sums into exclusive prefixes.
+  // sequences [t*bpt, (t+1)*bpt) (independent loads, one round trip); each
+  // warp scans its 32 sums in parallel, and every thread adds the totals of
+  // the warps before its own to get its exclusive prefix.
   __shared__ long long s_psum[THREADS];
   __shared__ long long s_pexc[THREADS];
+  __shared__ long long s_wtot[THREADS / 32];
   const int bpt = (p.B + THREADS - 1) / THREADS;
   {
     long long mysum = 0;
@@ -445,17 +447,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       long long t0;
       mysum += (seq_len<LAYOUT>(p, b, &t0) + PAGE - 1) / PAGE;
     }
+    const long long inc = warp_incl_scan(mysum, lane);
+    if (lane == 31) s_wtot[warp] = inc;
+    __syncthreads();
+    long long base = 0;
+    for (int w = 0; w < warp; ++w) base += s_wtot[w];
     s_psum[threadIdx.x] = mysum;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    long long run = 0;
-    for (int base = 0; base < THREADS; base += 32) {
-      const long long v = s_psum[base + lane];
-      const long long inc = warp_incl_scan(v, lane);
-      s_pexc[base + lane] = run + inc - v;
-      run += __shfl_sync(0xffffffffu, inc, 31);
-    }
+    s_pexc[threadIdx.x] = base + inc - mysum;
   }
   __syncthreads();
 #ifdef FK_TRACE
@@ -1040,6 +1038,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 
     // Blocks of 16 rows of this warp in the stage (two at D = 64).
     constexpr int NBLK = C::TILE / 64;
+#ifdef FK_EXP_NOMATH
+    if (false)
+#endif
 #pragma unroll
     for (int blk = 0; blk < NBLK; ++blk) {
       const int bo = blk * (WPH * 16);  // row offset of the block
@@ -1067,10 +1068,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
         const uint32_t wb[8] = {blo.x, blo.y, blo.z, blo.w, bhi.x, bhi.y, bhi.z, bhi.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint32_t a0 = e4m3x2_to_f16x2(wa[j]);
-          const uint32_t a2 = e4m3x2_to_f16x2(wa[j] >> 16);
-          const uint32_t a1 = e4m3x2_to_f16x2(wb[j]);
-          const uint32_t a3 = e4m3x2_to_f16x2(wb[j] >> 16);
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_f16x2x2(wa[j], a0, a2);
+          e4m3x4_to_f16x2x2(wb[j], a1, a3);
           if (j & 1) mma16816<false>(s2, a0, a1, a2, a3, qb[j][0], qb[j][1]);
           else mma16816<false>(s, a0, a1, a2, a3, qb[j][0], qb[j][1]);
         }
@@ -1092,7 +1092,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 #pragma unroll
       for (int i = 0; i < 4; ++i) s[i] += s2[i];
       // ---- online softmax (log2 domain), heads 2t and 2t+1
-      const bool okA = tok_ok(rowA), okB = tok_ok(rowB);
+      bool okA = true, okB = true;
+      if (partial) {
+        okA = tok_ok(rowA);
+        okB = tok_ok(rowB);
+      }
       const float x0 = okA ? s[0] * qk_scale : NEG_INF;
       const float x1 = okA ? s[1] * qk_scale : NEG_INF;
       const float x2 = okB ? s[2] * qk_scale : NEG_INF;
@@ -1146,8 +1150,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           const uint32_t sel = (i & 1) ? 0x7362u : 0x5140u;
           const uint32_t u01 = __byte_perm(w0[i >> 1], w1[i >> 1], sel);
           const uint32_t u89 = __byte_perm(w2[i >> 1], w3[i >> 1], sel);
-          mma16816<false>(acc[i], e4m3x2_to_f16x2(u01), e4m3x2_to_f16x2(u01 >> 16), e4m3x2_to_f16x2(u89),
-                          e4m3x2_to_f16x2(u89 >> 16), pb0, pb1);
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_f16x2x2(u01, a0, a1);
+          e4m3x4_to_f16x2x2(u89, a2, a3);
+          mma16816<false>(acc[i], a0, a1, a2, a3, pb0, pb1);
         }
       } else {
         uint32_t mk01 = 0xffffffffu, mk89 = 0xffffffffu;

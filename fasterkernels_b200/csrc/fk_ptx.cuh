@@ -172,6 +172,15 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v16) {
   return d;
 }
 
+// Four e4m3 bytes to two f16x2 registers: bytes 0,1 -> lo, bytes 2,3 -> hi.
+// The 32-bit word is split into its 16-bit halves inside the asm block, so
+// no shift is needed to reach the upper pair.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (BF16) {
