@@ -60,6 +60,10 @@ constexpr int PAGE = 16;       // tokens per granule (= page size)
 constexpr int MIN_PER = 4;     // minimum granules per CTA (one tile)
 constexpr int FK_EMPTY = -1;   // internal: common_checks found an empty batch
 constexpr float LOG2E = 1.4426950408889634f;
+// log2 headroom before the running max is moved (see the consumers); bf16 P
+// keeps the exact running max (0): its 8-bit mantissa leaves no slack in the
+// reference's 1e-3 tolerance.
+constexpr float LAZY_MAX_F16 = 8.f;
 constexpr float NEG_INF = -__builtin_huge_valf();
 
 enum Layout { VARLEN = 0, DENSE = 1, PAGED = 2 };
@@ -1055,6 +1059,16 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       float s[4] = {0.f, 0.f, 0.f, 0.f};
       float s2[4] = {0.f, 0.f, 0.f, 0.f};  // odd k-steps: two independent MMA chains
       int rowA, rowB;
+      // e4m3: this block's V rows are loaded up front, so that the loads are
+      // in flight while QK^T and the softmax run (PV waits only on P)
+      uint4 vx[FP8 ? 4 : 1];
+      if constexpr (FP8) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int row = r0b + t + 4 * (r & 1) + 8 * (r >> 1);
+          vx[r] = lds128(sV + TL::row_off(hk, row) + ((cg ^ (row & 7)) << 4));
+        }
+      }
       if constexpr (FP8) {
         rowA = (prow + bo);
         rowB = (prow + bo) + 8;
@@ -1101,25 +1115,26 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       const float x1 = okA ? s[1] * qk_scale : NEG_INF;
       const float x2 = okB ? s[2] * qk_scale : NEG_INF;
       const float x3 = okB ? s[3] * qk_scale : NEG_INF;
-      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+      // The running max moves only when a logit exceeds it by more than
+      // LAZY_MAX (log2 units): the warp-wide max reduction and the rescale
+      // are skipped otherwise, and P = 2^(x - m) stays below 2^LAZY_MAX
+      // (well inside f16 range).  Any reference m gives the same softmax once
+      // acc and l are normalised together; only the rounding differs.
+      constexpr float LAZY_MAX = MBF16 ? 0.f : LAZY_MAX_F16;
+      float al0 = 1.f, al1 = 1.f;
+      const bool grow = fmaxf(x0, x2) > m[0] + LAZY_MAX || fmaxf(x1, x3) > m[1] + LAZY_MAX;
+      if (__any_sync(0xffffffffu, grow)) {
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
 #pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-      }
-      const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
-      const float b0s = (mn0 == NEG_INF) ? 0.f : mn0;
-      const float b1s = (mn1 == NEG_INF) ? 0.f : mn1;
-      const float al0 = exp2f(m[0] - b0s), al1 = exp2f(m[1] - b1s);
-      const float p0 = exp2f(x0 - b0s), p1 = exp2f(x1 - b1s);
-      const float p2 = exp2f(x2 - b0s), p3 = exp2f(x3 - b1s);
-      l[0] = l[0] * al0 + (p0 + p2);
-      l[1] = l[1] * al1 + (p1 + p3);
-      m[0] = mn0;
-      m[1] = mn1;
-      // Rescale only when some running max of the warp moved (after the first
-      // tiles it rarely does); a factor of exactly 1 would leave acc as is.
-      if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+        for (int o = 4; o < 32; o <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+        al0 = exp2f(m[0] - ((mn0 == NEG_INF) ? 0.f : mn0));
+        al1 = exp2f(m[1] - ((mn1 == NEG_INF) ? 0.f : mn1));
+        m[0] = mn0;
+        m[1] = mn1;
 #pragma unroll
         for (int i = 0; i < KD; ++i) {
           acc[i][0] *= al0;
@@ -1128,6 +1143,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           acc[i][3] *= al1;
         }
       }
+      const float b0s = (m[0] == NEG_INF) ? 0.f : m[0];
+      const float b1s = (m[1] == NEG_INF) ? 0.f : m[1];
+      const float p0 = exp2f(x0 - b0s), p1 = exp2f(x1 - b1s);
+      const float p2 = exp2f(x2 - b0s), p3 = exp2f(x3 - b1s);
+      l[0] = l[0] * al0 + (p0 + p2);
+      l[1] = l[1] * al1 + (p1 + p3);
       // P^T as the B operand: transpose the 8x8 (token x head) blocks.
       const uint32_t pb0 = movmatrix_t(pack2<MBF16>(p0, p1));
       const uint32_t pb1 = movmatrix_t(pack2<MBF16>(p2, p3));
@@ -1138,7 +1159,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const int row = r0b + t + 4 * (r & 1) + 8 * (r >> 1);
-          x[r] = lds128(sV + TL::row_off(hk, row) + ((cg ^ (row & 7)) << 4));
+          x[r] = vx[r];
           if (partial && !tok_ok(row)) x[r] = make_uint4(0u, 0u, 0u, 0u);
         }
         const uint32_t w0[4] = {x[0].x, x[0].y, x[0].z, x[0].w};
