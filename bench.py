@@ -349,6 +349,9 @@ def measure_strong(args, rank, world, local_rank, device):
         import torch.distributed as dist
         torch.cuda.synchronize()
         dist.barrier()
+        gather_outputs(wl["out"], wl["indices"], wl["batch"])  # warm-up (first use of all_gather)
+        torch.cuda.synchronize()
+        dist.barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
