@@ -76,7 +76,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 template <int KV, int HP, int D, bool CP>
 constexpr size_t smem_bytes() {
   using C = KvCfg<KV, D, CP>;
-  return 1024 + C::STAGES * (C::STAGE_BYTES + sizeof(Meta) + sizeof(uint32_t) * HP * GPAD * 64 + 2 * sizeof(uint64_t)) +
+  return 1024 + C::STAGES * (C::STAGE_BYTES + sizeof(Meta) + 2 * sizeof(uint64_t)) +
+         C::QSLOTS * (sizeof(uint32_t) * HP * GPAD * 64 + sizeof(uint64_t)) +
          C::NSLOT * (sizeof(EpiSlot) + sizeof(Meta) + 2 * sizeof(uint64_t));
 }
 

@@ -94,6 +94,9 @@ struct KvCfg {
   static constexpr int NSLOT = (FP8 || CP) ? 1 : 2;          // epilogue slots (shared-memory budget)
   static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   static constexpr int MINB = (FP8 || CP) ? 2 : 1;           // resident CTAs per SM (at least)
+  // Q slots: each segment's Q rows are staged in one of two slots, released
+  // by the consumers once they hold them in registers.
+  static constexpr int QSLOTS = 2;
 };
 
 // One epilogue slot: the four consumer warps' online-softmax states of a
@@ -128,7 +131,7 @@ struct TileLayout {
 };
 
 struct Meta {
-  int b, h, tok, valid, flags, seg, bad, c0, nseg, pad[3];
+  int b, h, tok, valid, flags, seg, bad, c0, nseg, qslot, pad[2];
 };
 
 // Workspace layout (bytes), a function of the workspace SIZE W so that every
@@ -375,11 +378,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
   EpiSlot* eslot = reinterpret_cast<EpiSlot*>(smem + C::STAGES * C::STAGE_BYTES);  // [NSLOT]
   Meta* emeta = reinterpret_cast<Meta*>(eslot + C::NSLOT);                         // [NSLOT]
   Meta* meta = emeta + C::NSLOT;                                                   // [STAGES]
-  uint32_t* qstage = reinterpret_cast<uint32_t*>(meta + C::STAGES);                // [STAGES][QWORDS]
-  uint64_t* full = reinterpret_cast<uint64_t*>(qstage + C::STAGES * QWORDS);       // [STAGES]
+  uint32_t* qstage = reinterpret_cast<uint32_t*>(meta + C::STAGES);                // [QSLOTS][QWORDS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(qstage + C::QSLOTS * QWORDS);       // [STAGES]
   uint64_t* empty = full + C::STAGES;                                              // [STAGES]
   uint64_t* efull = empty + C::STAGES;                                             // [NSLOT]
   uint64_t* eempty = efull + C::NSLOT;                                             // [NSLOT]
+  uint64_t* qempty = eempty + C::NSLOT;                                            // [QSLOTS]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -411,10 +415,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       mbar_init(smem_u32(&efull[s]), CWARPS * 32);
       mbar_init(smem_u32(&eempty[s]), ETHREADS);
     }
+    for (int s = 0; s < C::QSLOTS; ++s) mbar_init(smem_u32(&qempty[s]), CWARPS);
     fence_mbar_init();
   }
-  // Q rows 16-byte aligned: each segment's Q rows are copied raw into the
-  // stage's Q slot by cp.async, completing on the stage's full barrier with
+  // Q rows 16-byte aligned: each segment's Q rows are copied raw into one of
+  // the two Q slots by cp.async, completing on the stage's full barrier with
   // the KV tiles, and the consumers convert them to the MMA type (and apply
   // scale_q) as they load them; the padding rows (heads G..7) are zeroed
   // once, here.  Otherwise the producer converts Q through registers.
@@ -423,8 +428,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
   const int gmin = p.qc == 1 ? p.G : (CP && (p.qc & 1)) ? 0 : (p.G % 8 == 0 ? 8 : p.G % 8);
   if (q_async && gmin < GPAD) {
     const int npad = GPAD - gmin;
-    for (int u = threadIdx.x; u < C::STAGES * HP * npad * 16; u += THREADS) {
-      const int row = u >> 4, c = u & 15;  // row over (stage, head, padding head)
+    for (int u = threadIdx.x; u < C::QSLOTS * HP * npad * 16; u += THREADS) {
+      const int row = u >> 4, c = u & 15;  // row over (Q slot, head, padding head)
       const int sh = row / npad, j = gmin + row % npad;
       reinterpret_cast<uint4*>(qstage + sh * (GPAD * 64) + j * 64)[c] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -514,6 +519,16 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
         stage = 0;
         phase ^= 1u;
       }
+    };
+    // Q slot of the next segment (waits for the consumers to release it).
+    int qslot = 0;
+    uint32_t qphase = 0;
+    auto qacquire = [&]() -> bool {
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(smem_u32(&qempty[qslot]), qphase ^ 1u, p.wait_ns) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok && lane == 0) atomicOr(&hdr->status, FK_STATUS_TIMEOUT);
+      return ok != 0;
     };
 
     // Q words of the next item, prefetched into registers: lane owns words
@@ -643,8 +658,18 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           const long long tc2 = clock64();
           if (tr_f && lane == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][18] = gtimer();
 #endif
+          int mqslot = 0;
           if (tt == tbeg) {
-            uint32_t* qs = qstage + stage * QWORDS;
+            if (!qacquire()) {
+              alive = false;
+              break;
+            }
+            mqslot = qslot;
+            if (++qslot == C::QSLOTS) {
+              qslot = 0;
+              qphase ^= 1u;
+            }
+            uint32_t* qs = qstage + mqslot * QWORDS;
             if (q_async) {
               // the item's query rows of D * 2 bytes, 16 bytes per copy, into
               // 256-byte row slots
@@ -690,6 +715,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
             mt.bad = bad;
             mt.c0 = c0;
             mt.nseg = nseg;
+            mt.qslot = mqslot;
             mbar_arrive_expect_tx(fb, bytes);
           }
           armed |= 1u << stage;
@@ -1015,7 +1041,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       for (int i = 0; i < KD; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
       // the producer staged this item's Q rows (zero-padded to 8 heads) next
       // to the segment's first tile: raw rows (cp.async) or MMA-type pairs
-      const uint32_t* qrow = qstage + stage * QWORDS + hh * (GPAD * 64) + g * 64;
+      const uint32_t* qrow = qstage + mt.qslot * QWORDS + hh * (GPAD * 64) + g * 64;
 #pragma unroll
       for (int j = 0; j < KD; ++j) {
         int d0, d1;
@@ -1038,6 +1064,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           qb[j][1] = q_pair_to_mma<MBF16>(p, qrow[d1 >> 1], qscale);
         }
       }
+      // this warp holds its Q rows in registers: release the Q slot
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&qempty[mt.qslot]));
     }
 
     // Blocks of 16 rows of this warp in the stage (two at D = 64).
