@@ -89,19 +89,29 @@ inline int qc_for(int q_heads, int kv_heads) {
 }
 
 // KV heads per work item: 2 when kv_heads is even (one TMA box then covers
-// both heads of a page) and the group fits one item, else 1.
-// FK_DECODE_HP=1 in the environment forces single-head items (a tuning knob;
-// read once, applies to every layout so paged and contiguous results stay
-// bit-identical).
-inline int hp_for(int kv_heads, int qc = 1) {
-  static const int forced = [] {
+// both heads of a page) and the group fits one item, else 1; e4m3 KV with
+// kv_heads % 4 == 0, a group of 5..8 query heads and 16-byte-aligned Q rows
+// takes 4 (one 8 KB box per page and head quad: half the TMA issues per
+// byte).  Measured: config 5 (G = 8, paged) 1.4-2.5 % faster with 4;
+// config 4 (G = 4, paged) and its dense cache 2-5 % slower, so groups of at
+// most 4 keep 2.
+// FK_DECODE_HP=1 / =2 in the environment caps the heads per item (a tuning
+// knob; read once, applies to every layout so paged and contiguous results
+// stay bit-identical).
+inline int hp_for(int kv_heads, int qc = 1, int kv = -1, int q_al16 = 0, int group = 8) {
+  static const int cap = [] {
     const char* e = getenv("FK_DECODE_HP");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
+    return (e != nullptr && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 4;
   }();
-  if (forced == 1) return 1;
+  if (cap == 1) return 1;
   if (qc > 1) return 2;  // chunk pairs of one KV head
+  if (cap >= 4 && kv == FK_DTYPE_E4M3 && q_al16 && kv_heads % 4 == 0 && group > 4) return 4;
   return (kv_heads % 2 == 0) ? 2 : 1;
 }
+
+// Grid sizes a workspace is planned for: four-head items use two 16-slot
+// records per segment, so their layout is planned for twice the CTAs.
+inline int ws_ctas(int S, int hp) { return hp == 4 ? 2 * S : S; }
 
 // Rows per pipeline stage (tokens x item heads) of the kernel for (kv, D).
 inline uint32_t tile_rows(int kv, int head_dim) {
@@ -109,10 +119,7 @@ inline uint32_t tile_rows(int kv, int head_dim) {
 }
 
 // KV heads in one TMA box: chunk pairs load a single head.
-inline uint32_t box_heads(int kv_heads, int qc) {
-  const int hp = hp_for(kv_heads, qc);
-  return static_cast<uint32_t>((qc > 1) ? 1 : hp);
-}
+inline uint32_t box_heads(int hp, int qc) { return static_cast<uint32_t>((qc > 1) ? 1 : hp); }
 
 template <int KV, int LAYOUT, int HP, int D, bool CP, bool QC>
 int prepare_kernel(int device) {
@@ -145,9 +152,10 @@ int occupancy(int device, int* per_sm) {
 // footprint and launch bounds), so paged, dense and varlen calls plan
 // identical segments.
 int num_work_ctas(int device, int kv, int hp, int d = HEAD_DIM, bool cp = false) {
-  static int cache[64][3][2][2][2] = {};
+  static int cache[64][3][4][2][2] = {};
   static std::mutex mu;
-  if (device < 0 || device >= 64 || kv < 0 || kv > 2 || hp < 1 || hp > 2 || (cp && hp != 2)) return 0;
+  if (device < 0 || device >= 64 || kv < 0 || kv > 2 || hp < 1 || hp > 4 || hp == 3 || (cp && hp != 2)) return 0;
+  if (hp == 4 && kv != FK_DTYPE_E4M3) return 0;
   if (d != 128 && (d != 64 || kv == FK_DTYPE_E4M3)) return 0;
   const int di = d == 64 ? 0 : 1, ci = cp ? 1 : 0;
   {
@@ -164,7 +172,7 @@ int num_work_ctas(int device, int kv, int hp, int d = HEAD_DIM, bool cp = false)
   int rc;
   if (kv == FK_DTYPE_F16) rc = d == 64 ? FK_OCC_D(FK_DTYPE_F16, 64) : FK_OCC_D(FK_DTYPE_F16, 128);
   else if (kv == FK_DTYPE_BF16) rc = d == 64 ? FK_OCC_D(FK_DTYPE_BF16, 64) : FK_OCC_D(FK_DTYPE_BF16, 128);
-  else rc = FK_OCC_D(FK_DTYPE_E4M3, 128);
+  else rc = hp == 4 ? FK_OCC(FK_DTYPE_E4M3, 4, 128, false) : FK_OCC_D(FK_DTYPE_E4M3, 128);
 #undef FK_OCC_D
 #undef FK_OCC
   if (prev != device) cudaSetDevice(prev);
@@ -275,16 +283,16 @@ int launch_one(const Params& p, int S, int device, cudaStream_t stream) {
 
 template <int LAYOUT>
 int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) {
-  const int hp = hp_for(p.kv_heads, p.qc);
+  const int hp = hp_for(p.kv_heads, p.qc, kv, p.q_al16, p.G);
   const bool cp = hp == 2 && p.qc > 1;  // chunk pairs
   const int S = num_work_ctas(device, kv, hp, p.head_dim, cp);
   if (S <= 0) return fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
   p.num_ctas = S;
   const int kvq = p.kv_heads * p.qc;  // (KV head, query chunk) pairs per sequence
-  const WsLayout wl(ws_bytes, p.B, kvq, S);
+  const WsLayout wl(ws_bytes, p.B, kvq, ws_ctas(S, hp));
   if (!wl.fits(ws_bytes, p.B, kvq))
     return fail(FK_ERR_WORKSPACE, "workspace too small: %zu bytes < %zu required", ws_bytes,
-                WsLayout::min_bytes(p.B, kvq, S));
+                WsLayout::min_bytes(p.B, kvq, ws_ctas(S, hp)));
   p.ws_cnt = static_cast<long long>(wl.cnt);
   p.ws_ml = static_cast<long long>(wl.ml);
   p.ws_acc = static_cast<long long>(wl.acc);
@@ -301,6 +309,7 @@ int launch(Params& p, int kv, int device, size_t ws_bytes, cudaStream_t stream) 
   int rc;
   if (kv == FK_DTYPE_F16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_F16, 64, false) : FK_L_D(FK_DTYPE_F16, 128, false);
   else if (kv == FK_DTYPE_BF16) rc = p.head_dim == 64 ? FK_L_D(FK_DTYPE_BF16, 64, false) : FK_L_D(FK_DTYPE_BF16, 128, false);
+  else if (hp == 4) rc = qconv ? FK_L(FK_DTYPE_E4M3, 4, 128, false, true) : FK_L(FK_DTYPE_E4M3, 4, 128, false, false);
   else rc = qconv ? FK_L_D(FK_DTYPE_E4M3, 128, true) : FK_L_D(FK_DTYPE_E4M3, 128, false);
 #undef FK_L_D
 #undef FK_L
@@ -368,10 +377,20 @@ extern "C" size_t fk_decode_workspace_bytes_gqa(int device, int batch, int q_hea
   }
   const int qc = qc_for(q_heads, kv_heads);
   const int hp = hp_for(kv_heads, qc);
-  const int S = num_work_ctas_any_d(device, kv_dtype, hp, hp == 2 && qc > 1);
+  int S = num_work_ctas_any_d(device, kv_dtype, hp, hp == 2 && qc > 1);
   if (S <= 0) {
     fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
     return 0;
+  }
+  // an e4m3 call may run four-head items (it depends on Q's alignment)
+  const int hp4 = hp_for(kv_heads, qc, kv_dtype, 1, q_heads / kv_heads);
+  if (hp4 == 4) {
+    const int S4 = num_work_ctas(device, kv_dtype, 4);
+    if (S4 <= 0) {
+      fail(FK_ERR_CUDA, "could not size the persistent grid on device %d", device);
+      return 0;
+    }
+    S = S > ws_ctas(S4, 4) ? S : ws_ctas(S4, 4);
   }
   return WsLayout::min_bytes(batch, kv_heads * qc, S);
 }
@@ -404,8 +423,8 @@ int varlen_prepare(Params& p, int* device, const void* q, const void* k_varlen, 
               nullptr, workspace);
   p.lens = cu_seqlens_k;
   const uint64_t T = static_cast<uint64_t>(total_tokens > 0 ? total_tokens : 1);
-  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
-  const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads), dtype, p.q_al16, q_heads / kv_heads));
+  const uint32_t hb = box_heads(static_cast<int>(hp), qc_for(q_heads, kv_heads));
   // 16-bit rows as (64 dims, T rows, D/64 halves [128 B apart], heads): one
   // box {64, 64/hp, D/64, hp} per stage lands as [head][half][rows][64].
   const uint32_t nh = static_cast<uint32_t>(head_dim / 64);
@@ -462,8 +481,8 @@ extern "C" int fk_flash_decode_gqa_hf_dense(const void* q, const void* k_cache, 
   p.lens = cache_lens;
   p.starts = start_k_offsets;
   p.max_tokens = max_seqlen;
-  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
-  const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads), kv_dtype, p.q_al16, q_heads / kv_heads));
+  const uint32_t hb = box_heads(static_cast<int>(hp), qc_for(q_heads, kv_heads));
   const uint64_t Bd = static_cast<uint64_t>(batch > 0 ? batch : 1);
   if (kv_dtype == FK_DTYPE_E4M3) {
     // (128 dims, S rows, heads, batch): box {128, 64/hp, hp, 1} -> [head][rows][128]
@@ -522,8 +541,8 @@ extern "C" int fk_paged_flash_decode(const void* q, const void* k_pool, const vo
   p.bt_sb = bt_b;
   p.max_blocks = max_blocks;
   p.num_pages = static_cast<int>(num_pages);
-  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads)));
-  const uint32_t hb = box_heads(kv_heads, qc_for(q_heads, kv_heads));
+  const uint32_t hp = static_cast<uint32_t>(hp_for(kv_heads, qc_for(q_heads, kv_heads), kv_dtype, p.q_al16, q_heads / kv_heads));
+  const uint32_t hb = box_heads(static_cast<int>(hp), qc_for(q_heads, kv_heads));
   if (kv_dtype == FK_DTYPE_E4M3) {
     // [P, KVH, 16, 128] bytes: one box {128, 16, hp, 1} per page -> [head][16][128]
     const uint64_t dims[4] = {HEAD_DIM, PAGE, static_cast<uint64_t>(kv_heads), static_cast<uint64_t>(num_pages)};

@@ -54,8 +54,11 @@ constexpr int CWARPS = 4;      // consumer warps, 16 tokens of each tile apiece
 constexpr int EWARPS = 2;      // epilogue warps: segment merge / output / partials
 constexpr int THREADS = (CWARPS + 1 + EWARPS) * 32;
 constexpr int ETHREADS = EWARPS * 32;
-constexpr int HPMAX = 2;       // KV heads per work item (2 when kv_heads is even)
-constexpr int GMAX = HPMAX * 8; // query-head slots per segment record
+constexpr int HPMAX = 2;       // KV heads per work item of the 16-bit kernels (2 when kv_heads is even)
+constexpr int GMAX = HPMAX * 8; // query-head slots per workspace record
+// e4m3 KV with kv_heads % 4 == 0 and groups of at most 8 query heads runs four
+// KV heads per item (one 8 KB TMA box per page instead of two 4 KB boxes);
+// its segment record spans two consecutive 16-slot records.
 constexpr int PAGE = 16;       // tokens per granule (= page size)
 constexpr int MIN_PER = 4;     // minimum granules per CTA (one tile)
 constexpr int FK_EMPTY = -1;   // internal: common_checks found an empty batch
@@ -236,6 +239,26 @@ __device__ __forceinline__ int items_per_seq(const Params& p) {
   return HP == 2 ? p.kv_heads * ((p.qc + 1) >> 1) : p.kv_heads * p.qc;
 }
 
+// Query row r (< item_rows) of item hi -> head slot hh and query head j
+// within the slot.  Four-head items only exist for groups of at most 8
+// query heads (one chunk).
+template <int HP>
+__device__ __forceinline__ int item_rows(const Params& p, int hi) {
+  if constexpr (HP == 4) return 4 * p.G;
+  else return item_g<HP>(p, hi, 0) + (HP == 2 ? item_g<HP>(p, hi, 1) : 0);
+}
+template <int HP>
+__device__ __forceinline__ void item_row(const Params& p, int hi, int r, int& hh, int& j) {
+  if constexpr (HP == 4) {
+    hh = r / p.G;
+    j = r - hh * p.G;
+  } else {
+    const int g0 = item_g<HP>(p, hi, 0);
+    hh = r < g0 ? 0 : 1;
+    j = r < g0 ? r : r - g0;
+  }
+}
+
 // Effective length of sequence b and the coordinate of its first token.
 template <int LAYOUT>
 __device__ __forceinline__ int seq_len(const Params& p, int b, long long* tok0) {
@@ -363,6 +386,8 @@ __device__ __forceinline__ unsigned long long gtimer() {
 template <int KV, int LAYOUT, int HP, int D, bool CP, bool QC>
 __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_kernel(const __grid_constant__ Params p) {
   static_assert(!CP || HP == 2, "chunk pairs fill the two head slots of an item");
+  static_assert(HP != 4 || (KV == FK_DTYPE_E4M3 && !CP), "four-head items are an e4m3 kernel");
+  constexpr int GSR = (HP == 4) ? 4 * GPAD : GMAX;  // query-head slots per segment record
   static_assert(!QC || KV == FK_DTYPE_E4M3, "16-bit KV takes Q of its own type");
   using C = KvCfg<KV, D, CP>;
   using TL = TileLayout<KV, LAYOUT, HP, D, CP>;
@@ -677,18 +702,19 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
               const long long qb0 = static_cast<long long>(b) * p.q_sb;
               const int qes = (p.q_dtype == FK_DTYPE_E4M3) ? 1 : 2;  // Q bytes per element
               const int nch = D * qes / 16;                          // 16-byte copies per row
-              const int g0 = item_g<HP>(p, hi, 0), g1 = HP == 2 ? item_g<HP>(p, hi, 1) : 0;
-              for (int u = lane; u < (g0 + g1) * nch; u += 32) {
+              const int nrow = item_rows<HP>(p, hi);
+              for (int u = lane; u < nrow * nch; u += 32) {
                 const int r = u / nch, c = u % nch;
-                const int hh = r < g0 ? 0 : 1, j = r < g0 ? r : r - g0;
+                int hh, j;
+                item_row<HP>(p, hi, r, hh, j);
                 const int qh = item_q<HP>(p, hi, hh, j);
                 cp_async16(qd + (hh * GPAD + j) * 256 + c * 16,
                            static_cast<const unsigned char*>(p.q) +
                                (qb0 + static_cast<long long>(qh) * p.q_sh) * qes + c * 16);
               }
               cp_async_mbar_arrive(fb);
-            } else {
-              // Q rows of the item -> qstage[stage] as packed MMA-type pairs,
+            } else if constexpr (HP != 4) {  // (four-head items always take the cp.async path)
+              // Q rows of the item -> the Q slot as packed MMA-type pairs,
               // from the registers prefetched one item ahead
               if (qpre_b != b || qpre_h != hi) q_prefetch(b, hi);
 #pragma unroll
@@ -855,10 +881,11 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       // One unit per thread and round: query head hd of KV head hh (head
       // slot u / 8), dims (u % 8) * 4 + 32 k, k < D / 32 (a quarter warp reads
       // 128 contiguous bytes of the slot: no bank conflicts).
-      const int g0 = item_g<HP>(p, mt.h, 0), g1 = HP == 2 ? item_g<HP>(p, mt.h, 1) : 0;
-      for (int u = et; u < (g0 + g1) * 8; u += ETHREADS) {
+      const int nrow = item_rows<HP>(p, mt.h);
+      for (int u = et; u < nrow * 8; u += ETHREADS) {
         const int r = u >> 3, d4 = (u & 7) * 4;
-        const int hh = r < g0 ? 0 : 1, hd = r < g0 ? r : r - g0;
+        int hh, hd;
+        item_row<HP>(p, mt.h, r, hh, hd);
         float M = NEG_INF;
 #pragma unroll
         for (int w = 0; w < WPH; ++w) M = fmaxf(M, E.cm[hh * WPH + w][hd]);
@@ -894,10 +921,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
                        norm_out(A[k].z, e, Lf, sv), norm_out(A[k].w, e, Lf, sv));
           }
         } else {
-          float4* dst = reinterpret_cast<float4*>(&ws_acc[(static_cast<long long>(mt.seg) * GMAX + hs) * HEAD_DIM + d4]);
+          float4* dst = reinterpret_cast<float4*>(&ws_acc[(static_cast<long long>(mt.seg) * GSR + hs) * HEAD_DIM + d4]);
 #pragma unroll
           for (int k = 0; k < D / 32; ++k) dst[8 * k] = A[k];
-          if ((u & 7) == 0) ws_ml[static_cast<long long>(mt.seg) * GMAX + hs] = make_float2(M, L);
+          if ((u & 7) == 0) ws_ml[static_cast<long long>(mt.seg) * GSR + hs] = make_float2(M, L);
         }
       }
       // the slot is consumed: give it back to the consumers
@@ -918,9 +945,10 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       __threadfence();
       // All head slots in parallel: unit u = (slot u / KD, dims (u % KD) * 16
       // .. +16); each thread merges its units with 4 segments' loads in flight.
-      for (int u = et; u < (g0 + g1) * KD; u += ETHREADS) {
+      for (int u = et; u < nrow * KD; u += ETHREADS) {
         const int r = u / KD, d0 = (u % KD) * 16;
-        const int hh = r < g0 ? 0 : 1, hd = r < g0 ? r : r - g0;
+        int hh, hd;
+        item_row<HP>(p, mt.h, r, hh, hd);
         const int hs = hh * GPAD + hd;
         float M = NEG_INF, L = 0.f;
         float A[16];
@@ -933,8 +961,8 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
           for (int v = 0; v < 4; ++v) {
             const long long sg = item + mt.c0 + c + v;
             const bool ok = c + v < mt.nseg;
-            ml[v] = ok ? __ldcg(&ws_ml[sg * GMAX + hs]) : make_float2(NEG_INF, 0.f);
-            const float4* src = reinterpret_cast<const float4*>(&ws_acc[(sg * GMAX + hs) * HEAD_DIM + d0]);
+            ml[v] = ok ? __ldcg(&ws_ml[sg * GSR + hs]) : make_float2(NEG_INF, 0.f);
+            const float4* src = reinterpret_cast<const float4*>(&ws_acc[(sg * GSR + hs) * HEAD_DIM + d0]);
 #pragma unroll
             for (int i = 0; i < 4; ++i) av[v][i] = ok ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
@@ -1295,7 +1323,9 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
   FK_KERNELS_LAYOUTS(X, KVT, 2, DD, true, QQ)
 #define FK_KERNELS_F16(X) FK_KERNELS_HP(X, FK_DTYPE_F16, 64, false) FK_KERNELS_HP(X, FK_DTYPE_F16, 128, false)
 #define FK_KERNELS_BF16(X) FK_KERNELS_HP(X, FK_DTYPE_BF16, 64, false) FK_KERNELS_HP(X, FK_DTYPE_BF16, 128, false)
-#define FK_KERNELS_E4M3(X) FK_KERNELS_HP(X, FK_DTYPE_E4M3, 128, false) FK_KERNELS_HP(X, FK_DTYPE_E4M3, 128, true)
+#define FK_KERNELS_E4M3(X)                                                                                  \
+  FK_KERNELS_HP(X, FK_DTYPE_E4M3, 128, false) FK_KERNELS_HP(X, FK_DTYPE_E4M3, 128, true)                   \
+  FK_KERNELS_LAYOUTS(X, FK_DTYPE_E4M3, 4, 128, false, false) FK_KERNELS_LAYOUTS(X, FK_DTYPE_E4M3, 4, 128, false, true)
 #define FK_KERNEL_DECL(KVT, L, H, DD, CC, QQ) \
   extern template __global__ void fk::decode_split_kernel<KVT, L, H, DD, CC, QQ>(const __grid_constant__ fk::Params);
 #define FK_KERNEL_INST(KVT, L, H, DD, CC, QQ) \

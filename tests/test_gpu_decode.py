@@ -758,8 +758,10 @@ def test_head_dim_64_append_then_decode(dev):
 def test_fp8_query_paged_raw_copy_matches_register_path(dev):
     # an e4m3 query with scale_q, as the reference's FP8 entry takes it: rows
     # aligned to 16 bytes are copied raw and converted by the consumers; an
-    # unaligned strided view goes through the producer's registers.  Same
-    # formula, so the outputs are bit-identical.
+    # unaligned strided view goes through the producer's registers.  Aligned
+    # rows also let the kernel take four KV heads per work item (two for the
+    # register path), so the two split the work differently and agree to
+    # rounding.
     lens = [1, 33, 1500, 0, 4097, 777]
     d = W.make_varlen(lens, 32, 8, torch.float32, dev, seed=77, sinks=True)
     k8, sk = W.quantize_e4m3(d["k"])
@@ -775,7 +777,7 @@ def test_fp8_query_paged_raw_copy_matches_register_path(dev):
     qv = qbig.view(torch.float8_e4m3fn)[:, :, :128]  # head stride 136 bytes: not 16-byte aligned
     out_v = fk.paged_flash_decode(qv, kp, vp, bt, sl, 16, s_aux=d["s_aux"], scale_q=sq, scale_k=sk, scale_v=sv,
                                   out_dtype=torch.float16)
-    assert torch.equal(out, out_v)
+    close(out_v, out.float().cpu().numpy(), atol=1e-3, rtol=1e-3)
     qd = (q8.float() * sq).half()
     ref = O.decode_varlen(qd.float().cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
                           d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
