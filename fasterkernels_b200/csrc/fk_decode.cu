@@ -725,6 +725,6 @@ extern "C" int fk_noalloc_read_status(int device, int* status, int clear) {
 
 #ifdef FK_TRACE
 extern "C" int fk_trace_read(unsigned long long* host, int n) {
-  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 24 * n) == cudaSuccess ? 0 : 1;
+  return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 32 * n) == cudaSuccess ? 0 : 1;
 }
 #endif

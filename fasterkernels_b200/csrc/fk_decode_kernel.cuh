@@ -369,7 +369,7 @@ __device__ __forceinline__ float norm_out(float A, float e, float Lf, float sv) 
 // [start, first tile, consumer end (ns), segments, tiles, producer switch ns, producer acquire-wait ns,
 //  consumer wait ns at first tiles of segments, consumer wait ns at other tiles, epilogue end (ns),
 //  SM id, producer cycles in block-table lookup, in Q staging, in issue, per whole tile]
-__device__ unsigned long long g_trace[4096][24];
+__device__ unsigned long long g_trace[4096][32];
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
 
 #ifdef FK_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 4096) {
-    for (int i = 1; i < 24; ++i) g_trace[blockIdx.x][i] = 0;
+    for (int i = 1; i < 32; ++i) g_trace[blockIdx.x][i] = 0;
     g_trace[blockIdx.x][0] = gtimer();
     unsigned smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
@@ -873,7 +873,12 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][23] += te1 - te0;
 #endif
       const Meta mt = emeta[eb];
-      if (mt.flags & F_END) break;
+      if (mt.flags & F_END) {
+#ifdef FK_TRACE
+        if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][27] = gtimer();
+#endif
+        break;
+      }
       const EpiSlot& E = eslot[eb];
       const bool whole = (mt.flags & F_WHOLE) != 0;
       const long long item = static_cast<long long>(mt.b) * KVI + mt.h;
@@ -939,7 +944,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
       if (whole) continue;
       __threadfence();
       named_bar_sync(2, ETHREADS);
+#ifdef FK_TRACE
+      if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][24] = gtimer();  // partial stored, before the atomic
+#endif
       if (et == 0) s_last = (atomicAdd(&cnt[item], 1) == mt.nseg - 1) ? 1 : 0;
+#ifdef FK_TRACE
+      if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][25] = gtimer();  // atomic returned
+#endif
       named_bar_sync(2, ETHREADS);
       if (!s_last) continue;
       __threadfence();
@@ -998,6 +1009,13 @@ __global__ void __launch_bounds__(THREADS, KvCfg<KV, D, CP>::MINB) decode_split_
                      norm_out(A[i + 2], e, Lf, sv), norm_out(A[i + 3], e, Lf, sv));
       }
       if (et == 0) cnt[item] = 0;
+#ifdef FK_TRACE
+      if (et == 0 && blockIdx.x < 4096) {
+        g_trace[blockIdx.x][26] = gtimer();  // merge done
+        g_trace[blockIdx.x][28] += 1;
+        g_trace[blockIdx.x][29] = mt.nseg;
+      }
+#endif
     }
 #ifdef FK_TRACE
     if (et == 0 && blockIdx.x < 4096) g_trace[blockIdx.x][9] = gtimer();
