@@ -809,3 +809,61 @@ def test_bounded_wait_runs_out_and_reports_timeout(dev):
     close(out, ref, **F16_TOL)
     assert N.read_status(dev) == 0
     assert L.fk_debug_configure(10, 0) != 0  # out-of-range bound refused
+
+
+# ------------------------------------------------- four KV heads per item
+@pytest.mark.parametrize("G,kvh,qdt", [(5, 4, torch.float16), (6, 8, torch.float16), (8, 4, torch.bfloat16),
+                                       (8, 8, torch.float8_e4m3fn)])
+def test_fp8_four_head_items_paged_dense_and_oracle(dev, G, kvh, qdt):
+    # e4m3 KV with kv_heads % 4 == 0 and groups of 5..8 query heads runs four
+    # KV heads per work item (one TMA box per page and head quad); Q of
+    # another type is converted by the consumers; paged == dense bits
+    lens = [1, 15, 16, 17, 700, 0, 4097, 2049]
+    d = W.make_varlen(lens, G * kvh, kvh, torch.float32, dev, seed=90 + G, sinks=True)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    if qdt == torch.float8_e4m3fn:
+        q, sq = fk.quantize_to_fp8(d["q"])
+        qref = (q.float() * sq).half().float()
+    else:
+        q, sq = d["q"].to(qdt), None
+        qref = q.float()
+    sl = torch.tensor(lens, dtype=torch.int32, device=dev)
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=G)
+    outp = fk.paged_flash_decode(q, kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn), bt, sl, 16,
+                                 s_aux=d["s_aux"], scale_q=sq, scale_k=sk, scale_v=sv, out_dtype=torch.float16)
+    S = max(lens)
+    kc = torch.zeros(len(lens), kvh, S, 128, dtype=torch.uint8, device=dev)
+    vc = torch.zeros_like(kc)
+    cu = d["cu_seqlens"].tolist()
+    for b, L in enumerate(lens):
+        kc[b, :, :L] = k8.view(torch.uint8)[cu[b]:cu[b + 1]].transpose(0, 1)
+        vc[b, :, :L] = v8.view(torch.uint8)[cu[b]:cu[b + 1]].transpose(0, 1)
+    outd = fk.flash_decode_gqa_hf_fp8(q, kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn), sl, sq, sk, sv,
+                                      torch.float16, s_aux=d["s_aux"])
+    torch.cuda.synchronize()
+    assert torch.equal(outd, outp)
+    ref = O.decode_varlen(qref.cpu().numpy(), (k8.float() * sk).cpu().numpy(), (v8.float() * sv).cpu().numpy(),
+                          d["cu_seqlens"].cpu().numpy(), d["s_aux"].cpu().numpy())
+    close(outp, ref, atol=3e-3 if qdt == torch.float16 else 1e-2, rtol=1e-2)
+    assert N.read_status(dev) == 0
+
+
+def test_fp8_four_head_items_bad_pages(dev):
+    lens = [40, 300]
+    d = W.make_varlen(lens, 64, 8, torch.float32, dev, seed=95, sinks=False)
+    k8, sk = W.quantize_e4m3(d["k"])
+    v8, sv = W.quantize_e4m3(d["v"])
+    kp, vp, bt = W.varlen_to_paged(k8.view(torch.uint8), v8.view(torch.uint8), lens, 1.25, seed=3)
+    N.read_status(dev)
+    bt = bt.clone()
+    bt[1, 5] = kp.shape[0] + 7  # tokens 80..95 of sequence 1: outside the pool
+    out = fk.paged_flash_decode(d["q"].half(), kp.view(torch.float8_e4m3fn), vp.view(torch.float8_e4m3fn), bt,
+                                torch.tensor(lens, dtype=torch.int32, device=dev), 16, scale_k=sk, scale_v=sv)
+    torch.cuda.synchronize()
+    assert N.read_status(dev) & N.FK_STATUS_BAD_PAGE
+    keep = np.r_[0:80, 96:300]
+    k1 = (k8.float() * sk)[40:340][keep].cpu().numpy()
+    v1 = (v8.float() * sv)[40:340][keep].cpu().numpy()
+    ref = O.decode_varlen(d["q"][1:2].half().float().cpu().numpy(), k1, v1, np.array([0, len(keep)]))
+    close(out[1:2], ref, atol=3e-3, rtol=1e-2)
