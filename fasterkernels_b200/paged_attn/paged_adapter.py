@@ -47,6 +47,7 @@ class _Binding:
     seq_ids: List[int] = field(default_factory=list)
     write_prefill: bool = True
     lens: Optional[torch.Tensor] = None  # lengths of the step in progress (device)
+    bt: Optional[torch.Tensor] = None    # block-table rows of the step in progress (device)
 
 
 _BOUND = _Binding()
@@ -59,6 +60,7 @@ def set_paged_attention_cache(cache: Optional[PagedKVCache], seq_ids: List[int],
     _BOUND.seq_ids = list(seq_ids)
     _BOUND.write_prefill = bool(write_prefill)
     _BOUND.lens = None
+    _BOUND.bt = None
 
 
 def get_paged_attention_cache() -> Tuple[Optional[PagedKVCache], List[int]]:
@@ -75,17 +77,18 @@ def custom_paged_attention_forward(module, query_states, key_states, value_state
         if len(_BOUND.seq_ids) != bsz:
             raise ValueError(f"bound {len(_BOUND.seq_ids)} sequence ids for a batch of {bsz}")
         if layer == 0 or _BOUND.lens is None:
-            _, _, _BOUND.lens = cache.begin_step(_BOUND.seq_ids)
+            _BOUND.bt, _, _BOUND.lens = cache.begin_step(_BOUND.seq_ids)
         cache.append_kv_batch(layer, key_states[:, :, -1], value_states[:, :, -1])
         e4m3 = cache.dtype == torch.float8_e4m3fn
         out = paged_flash_decode(query_states.squeeze(2), cache.k_pool[layer], cache.v_pool[layer],
-                                 cache._step_bt, _BOUND.lens, PAGE_SIZE,
+                                 _BOUND.bt, _BOUND.lens, PAGE_SIZE,
                                  s_aux=_module_sinks(module, q_heads, query_states.device),
                                  scale_k=cache.k_scale if e4m3 else None, scale_v=cache.v_scale if e4m3 else None,
                                  out_dtype=query_states.dtype if e4m3 else None)
         if layer == cache.num_layers - 1:
             cache.end_step()
             _BOUND.lens = None
+            _BOUND.bt = None
         return out.unsqueeze(2), None
     if cache is not None and _BOUND.write_prefill and q_len > 1 and len(_BOUND.seq_ids) == bsz:
         for b, sid in enumerate(_BOUND.seq_ids):
