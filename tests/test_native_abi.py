@@ -69,3 +69,16 @@ def test_debug_hook_validates_its_arguments():
     assert L.fk_debug_configure(10, 0) == 1 and "wait_ns" in N.last_error()
     assert L.fk_debug_configure(4_000_000_000, 2) == 1 and "inject" in N.last_error()
     assert L.fk_debug_configure(4_000_000_000, 0) == 0  # the default: 4 s bound, no injection
+
+
+def test_custom_ops_are_registered_with_mutation_schemas():
+    # torch.compile traces the entry points through these ops; each declares
+    # the tensors it writes
+    import torch
+    import fasterkernels_b200  # noqa: F401  (registers the ops)
+    ns = torch.ops.fasterkernels_b200
+    for name, mutated in (("varlen_decode", {"out"}), ("dense_decode", {"out"}), ("paged_decode", {"out"}),
+                          ("paged_kv_append", {"k_pool", "v_pool", "positions", "status"})):
+        schema = getattr(ns, name).default._schema
+        written = {a.name for a in schema.arguments if a.alias_info is not None and a.alias_info.is_write}
+        assert written == mutated, (name, written)

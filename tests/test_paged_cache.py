@@ -99,3 +99,26 @@ def test_begin_end_step_host_bookkeeping():
     assert new_lens.tolist() == [16, 1] and c.seq_len(a) == 16
     c.begin_step([a])  # a crosses into its second page
     assert c.pages_used == 3 and int(c.block_table[a, 1]) >= 0
+
+
+def test_write_prefill_pages_and_reserve():
+    # the prompt of one layer lands token by token in its pages; reserve
+    # pre-allocates the pages later decode steps will use
+    c = PagedKVCache(num_layers=2, num_pages=20, max_seqs=2, max_blocks_per_seq=8, num_kv_heads=2, head_dim=4,
+                     dtype=torch.float32, device="cpu")
+    s = c.allocate_sequence()
+    k = torch.randn(2, 37, 4)
+    v = torch.randn(2, 37, 4)
+    c.write_prefill(s, 1, k, v, reserve=60)
+    assert c.seq_len(s) == 37
+    bt = c.get_block_table_tensor([s])[0]
+    assert (bt[:4] >= 0).all() and (bt[4:] == -1).all()  # ceil(60 / 16) pages
+    pages = bt[:3].tolist()
+    got_k = torch.cat([c.k_pool[1][p] for p in pages], dim=1)[:, :37]
+    got_v = torch.cat([c.v_pool[1][p] for p in pages], dim=1)[:, :37]
+    assert torch.equal(got_k, k) and torch.equal(got_v, v)
+    assert float(c.k_pool[0].abs().sum()) == 0.0  # other layers untouched
+    c.write_prefill(s, 0, k, v)  # the same prompt for layer 0: no new pages
+    assert c.get_block_table_tensor([s])[0].tolist() == bt.tolist() and c.seq_len(s) == 37
+    with pytest.raises(RuntimeError):
+        c.write_prefill(s, 0, torch.zeros(2, 200, 4), torch.zeros(2, 200, 4))  # > max_blocks_per_seq
